@@ -1,0 +1,248 @@
+/*
+ * va_cuda.h -- C ABI of libva_cuda, the B200 (sm_100a) exact-search library.
+ *
+ * This is the drop-in boundary for VectorAccelerate's exact flat k-NN path. Every entry point
+ * replaces one reference interface (Swift class/method; file:line relative to the
+ * VectorAccelerate project root) and keeps its argument meaning, result conventions and error
+ * behaviour:
+ *   - ids are uint32; 0xFFFFFFFF pads a result row when fewer than k candidates exist
+ *     (FusedL2TopKKernel.swift:155-172, SearchAndRetrieval.metal:151-155);
+ *   - squared L2 is returned (computeSqrt = false), ascending; inner product is returned
+ *     descending; cosine distance is 1 - similarity, ascending;
+ *   - every selection orders by (distance, id): equal distances keep the smaller id
+ *     (AdvancedTopK.metal:48-52, SearchAndRetrieval.metal:313-317);
+ *   - distance pads are +inf (minimum modes) and -inf (maximum modes).
+ *
+ * Conventions of this ABI:
+ *   - plain pointers and sizes only; device pointers are CUDA device addresses on the
+ *     context's device, host pointers are ordinary (pageable or pinned) memory;
+ *   - every function returns an int status: VA_OK (0) or a negative VA_ERR_* code, and never
+ *     aborts; va_last_error() returns a thread-local message naming the offending parameter and
+ *     its limit (IndexError.invalidInput messages, FusedL2TopKKernel.swift:52-85);
+ *   - work is enqueued on the context's stream (stream order replaces Metal's memoryBarrier);
+ *     va_synchronize() is the bounded wait that replaces Metal4Context.executeAndWait
+ *     (Core/Metal4Context.swift:342-410);
+ *   - there is no CPU fallback: without a usable GPU every call fails with VA_ERR_CUDA.
+ */
+#ifndef VA_CUDA_H
+#define VA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define VA_ABI_VERSION 1
+
+/* ------------------------------------------------------------------------------------------ */
+/* Status codes                                                                                */
+/* ------------------------------------------------------------------------------------------ */
+#define VA_OK 0
+#define VA_ERR_INVALID_ARG (-1) /* VectorError.invalidInput / IndexError.invalidInput           */
+#define VA_ERR_OOM (-2)         /* VectorError.bufferAllocationFailed                            */
+#define VA_ERR_CUDA (-3)        /* VectorError.computeFailed (commandBuffer.error)               */
+#define VA_ERR_NCCL (-4)        /* collective failure (no reference counterpart: single GPU)     */
+#define VA_ERR_TIMEOUT (-5)     /* a bounded host wait or a bounded device wait expired          */
+#define VA_ERR_UNSUPPORTED (-6) /* combination not supported by this build                       */
+
+/* Metrics (SupportedDistanceMetric subset on the flat path). */
+#define VA_METRIC_L2SQ 0   /* squared Euclidean, smaller is closer                                */
+#define VA_METRIC_COSINE 1 /* 1 - cos(q, x), smaller is closer                                    */
+#define VA_METRIC_IP 2     /* inner product, larger is closer                                      */
+
+/* Contraction precision of the fused search. Reduced-precision passes are always followed by an
+ * exact rerank of the candidates, so results equal the exact search's apart from stated ties. */
+#define VA_PREC_AUTO 0 /* BF16 tensor cores when the row layout allows, else FP32            */
+#define VA_PREC_FP32 1 /* exact fp32 SIMT contraction, chunked, no rerank needed             */
+#define VA_PREC_TF32 2 /* tcgen05 kind::tf32 on the fp32 rows + exact rerank                 */
+#define VA_PREC_BF16 3 /* tcgen05 kind::f16 (bf16) + exact rerank                            */
+
+/* Row element types of a database. */
+#define VA_DTYPE_F32 0
+#define VA_DTYPE_BF16 1
+
+/* Selection modes (Metal4SelectionMode, TopKSelectionKernel.swift:23-29). */
+#define VA_SELECT_MIN 0
+#define VA_SELECT_MAX 1
+
+/* Limits of this build (the reference caps d <= 768 and k <= 128:
+ * FusedL2TopKKernel.swift:39-42; TopKSelectionKernel.swift:60). */
+#define VA_MAX_DIM 4096
+#define VA_MAX_K 1024
+#define VA_MAX_SELECT_K 4096
+
+typedef struct va_context va_context;
+typedef struct va_database va_database;
+
+/* Context configuration (Metal4Configuration, Core/Metal4Context.swift:13-44). */
+typedef struct va_config {
+    int device;              /* CUDA device ordinal                                            */
+    unsigned int timeout_ms; /* limit of every bounded wait; 0 selects 120000                  */
+    void* stream;            /* optional cudaStream_t to enqueue on; NULL creates one          */
+} va_config;
+
+/* ------------------------------------------------------------------------------------------ */
+/* Errors, devices, contexts                                                                   */
+/* ------------------------------------------------------------------------------------------ */
+const char* va_last_error(void);
+int va_abi_version(void);
+int va_device_count(int* count);
+
+/* Replaces Metal4Context.init(configuration:) (Core/Metal4Context.swift:175-183). */
+int va_context_create(const va_config* cfg, va_context** out);
+int va_context_destroy(va_context* ctx);
+/* The cudaStream_t the context enqueues on. */
+int va_context_stream(va_context* ctx, void** stream);
+/* Bounded wait for all enqueued work, then a check of the device error word written by bounded
+ * device-side waits. Replaces executeAndWait's commit/wait/error check
+ * (Core/Metal4Context.swift:377-409). */
+int va_synchronize(va_context* ctx);
+/* Device time in ms of the last call that timed itself (GPUTimingInfo, Metal4Context.swift:48-65). */
+int va_last_gpu_time_ms(va_context* ctx, float* ms);
+/* Device times of the last va_knn_search on this context, measured with CUDA events on the
+ * context stream: the whole search and its dominant kernel (the tensor-core filter; 0 on the
+ * FP32 route). Valid once the search has completed (after va_synchronize). */
+int va_last_search_times(va_context* ctx, float* total_ms, float* kernel_ms);
+/* Profile the dominant kernel of the next `capacity` searches (a CUDA event pair per call on
+ * the context stream, no synchronisation between calls); va_profile_stop waits (bounded) and
+ * returns the summed kernel time and the number of profiled calls. */
+int va_profile_start(va_context* ctx, int capacity);
+int va_profile_stop(va_context* ctx, float* kernel_ms_total, int* calls);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Buffers: replace MTLBuffer / BufferToken (Core/BufferPool.swift:89-221,                     */
+/* Core/Metal4Context.swift:471-488). Caller-owned; free with va_buffer_free.                  */
+/* ------------------------------------------------------------------------------------------ */
+int va_buffer_alloc(va_context* ctx, size_t bytes, void** dptr);
+int va_buffer_free(va_context* ctx, void* dptr);
+int va_host_alloc(va_context* ctx, size_t bytes, void** hptr); /* pinned host memory */
+int va_host_free(va_context* ctx, void* hptr);
+/* Stream-ordered copies (host<->device or device<->device); asynchronous for pinned memory. */
+int va_buffer_upload(va_context* ctx, void* dst_dev, const void* src_host, size_t bytes);
+int va_buffer_download(va_context* ctx, void* dst_host, const void* src_dev, size_t bytes);
+int va_buffer_copy(va_context* ctx, void* dst_dev, const void* src_dev, size_t bytes);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Distance primitives (device pointers, fp32, stream-ordered)                                 */
+/* ------------------------------------------------------------------------------------------ */
+/* 1:1 pairs: out[p] = |a_p - b_p|^2 (or |a_p - b_p| when compute_sqrt).
+ * Replaces L2DistanceKernel.encode (Kernels/Metal4/L2DistanceKernel.swift:49-86). */
+int va_l2_distance_pairs(va_context* ctx, const float* a, const float* b, int64_t pairs, int dim,
+                         int compute_sqrt, float* out);
+/* 1:1 pairs: cosine similarity, or 1 - similarity when output_distance; 0 when a norm is 0.
+ * Replaces CosineSimilarityKernel.encode (Kernels/Metal4/CosineSimilarityKernel.swift:50-87). */
+int va_cosine_pairs(va_context* ctx, const float* a, const float* b, int64_t pairs, int dim,
+                    int output_distance, float* out);
+/* All-pairs matrix out[i*out_stride + j] for queries q[nq x dim], rows x[nx x dim]:
+ *   VA_METRIC_L2SQ: squared L2 (sqrt when flag)      -- l2_distance_kernel, L2Distance.metal:34-91
+ *   VA_METRIC_IP:   dot product (abs when flag)      -- DotProductKernel.encode,
+ *                                                       Kernels/Metal4/DotProductKernel.swift:226-275
+ *   VA_METRIC_COSINE: similarity (1 - sim when flag) -- cosine all-pairs, CosineSimilarity.metal */
+int va_distance_matrix(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
+                       int metric, int flag, float* out, int64_t out_stride);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Selection                                                                                   */
+/* ------------------------------------------------------------------------------------------ */
+/* Batch top-k of rows in[r*in_stride + i], i < n: sorted best-first by (value, index).
+ * Replaces TopKSelectionKernel.execute/select (Kernels/Metal4/TopKSelectionKernel.swift:228-411)
+ * and WarpOptimizedSelectionKernel (WarpOptimizedSelectionKernel.swift:250-863).
+ * k <= VA_MAX_SELECT_K. out rows have stride out_stride (>= k). */
+int va_topk_select(va_context* ctx, const float* in, int64_t batch, int64_t n, int64_t in_stride, int k,
+                   int mode, float* out_vals, uint32_t* out_ids, int64_t out_stride);
+/* Merge a running sorted top-k with a chunk's sorted top-kc whose ids are chunk-local (chunk_base
+ * is added). Replaces TopKMergeKernel (Kernels/Metal4/TopKMergeKernel.swift:18-127). Output may
+ * alias the running buffers. */
+int va_topk_merge(va_context* ctx, const float* run_vals, const uint32_t* run_ids, int k, const float* chunk_vals,
+                  const uint32_t* chunk_ids, int kc, uint32_t chunk_base, int64_t nq, int mode, float* out_vals,
+                  uint32_t* out_ids);
+/* Merge per-shard results gathered as [nshards][nq][k] (global ids) into the global top-k.
+ * The device merge after the NCCL allgather of a row-sharded search (no reference counterpart:
+ * the reference is single-GPU; its chunk merge is SearchAndRetrieval.metal:320-385). */
+int va_merge_shards(va_context* ctx, const float* vals, const uint32_t* ids, int nshards, int64_t nq, int k,
+                    int mode, float* out_vals, uint32_t* out_ids);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Database and fused search                                                                   */
+/* ------------------------------------------------------------------------------------------ */
+/* Create a resident database of n rows x dim (row-major, dtype VA_DTYPE_F32 or VA_DTYPE_BF16),
+ * copied from host (on_device = 0) or device memory. Replaces the storage buffer of
+ * GPUVectorStorage (Index/Internal/GPUVectorStorage.swift:52-100). id_base is added to every
+ * returned id (global ids of a row shard). At build time the library derives the tensor-core
+ * operand copy (bf16, normalised for cosine) and the row norms. */
+int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype,
+                 uint32_t id_base, va_database** out);
+int va_db_destroy(va_database* db);
+int va_db_info(const va_database* db, int64_t* n, int* dim, int* dtype);
+/* Device pointer of the database's original rows (fp32 or bf16 per dtype). */
+int va_db_rows(const va_database* db, const void** rows);
+
+/* Fused exact k-NN over the database: queries[nq x dim] fp32 (device), results sorted
+ * best-first into out_vals/out_ids [nq x k] (device). Replaces FusedL2TopKKernel.execute
+ * (Kernels/Metal4/FusedL2TopKKernel.swift:367-427) and the batch flat search
+ * AcceleratedVectorIndex.searchBatchGPU (Index/AcceleratedVectorIndex.swift:1278-1374), extended
+ * to cosine and inner product. rerank = candidate pool per query of the reduced-precision pass
+ * (0 = automatic). */
+int va_knn_search(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int metric,
+                  int precision, int rerank, float* out_vals, uint32_t* out_ids);
+/* Same, with HOST query and result buffers: copies in, searches, copies out and waits (bounded).
+ * This is the whole reference call (findNearestNeighbors, FusedL2TopKKernel.swift:439-529). */
+int va_knn_search_host(va_context* ctx, const va_database* db, const float* queries_host, int64_t nq, int k,
+                       int metric, int precision, int rerank, float* out_vals_host, uint32_t* out_ids_host);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Scalar quantization (ScalarQuantizationKernel, Kernels/Metal4/ScalarQuantizationKernel.swift;  */
+/* quantize_int8_kernel / dequantize_int8_kernel / int4, DataTransformations.metal:142-306)      */
+/* ------------------------------------------------------------------------------------------ */
+/* q = clamp(rint(x/scale + zp), -128, 127). When scales != NULL, channel c = i / (n/n_channels)
+ * uses scales[c] and zps[c] (zps may be NULL: 0). */
+int va_sq_quantize_int8(va_context* ctx, const float* x, int64_t n, float scale, int8_t zero_point,
+                        const float* scales, const int8_t* zps, int64_t n_channels, int8_t* out);
+int va_sq_dequantize_int8(va_context* ctx, const int8_t* in, int64_t n, float scale, int8_t zero_point,
+                          const float* scales, const int8_t* zps, int64_t n_channels, float* out);
+/* int4: two codes per byte, element 2i in the low nibble; range [-8, 7]. */
+int va_sq_quantize_int4(va_context* ctx, const float* x, int64_t n, float scale, int8_t zero_point, uint8_t* out);
+int va_sq_dequantize_int4(va_context* ctx, const uint8_t* in, int64_t n, float scale, int8_t zero_point,
+                          float* out);
+/* Global min and max of x (device reduction); out_minmax[2] is a device pointer. */
+int va_minmax(va_context* ctx, const float* x, int64_t n, float* out_minmax);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Binary quantization and Hamming (BinaryQuantizationKernel, HammingDistanceKernel)           */
+/* ------------------------------------------------------------------------------------------ */
+/* Pack bit b of word w = (x[i][32w+b] > threshold), LSB first (binaryQuantize,
+ * QuantizationShaders.metal:132-160; the shader fixes threshold = 0). out: n x ceil(dim/32). */
+int va_binary_quantize(va_context* ctx, const float* x, int64_t n, int dim, float threshold, uint32_t* out);
+/* Hamming matrix out[i*nx + j] = popcount(q_i ^ x_j) over `words` uint32 words
+ * (hamming_distance_batch, HammingDistance.metal:28-127). out_normalized (optional, may be
+ * NULL) receives distance / dim (hamming_distance_normalized, :242-321). */
+int va_hamming_matrix(va_context* ctx, const uint32_t* q, int64_t nq, const uint32_t* x, int64_t nx, int words,
+                      uint32_t* out, float* out_normalized, int dim);
+/* Fused Hamming k-NN: distances never materialised; results sorted by (distance, id)
+ * (replaces computeBitPacked + Metal4HammingResult.nearestNeighbors' CPU sort,
+ * HammingDistanceKernel.swift:114-120,313-363). */
+int va_hamming_knn(va_context* ctx, const uint32_t* q, int64_t nq, const uint32_t* x, int64_t nx, int words, int k,
+                   uint32_t* out_dists, uint32_t* out_ids);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Seeded synthetic data on the device (restates Tests/.../Utilities/TestRNG.swift:57-161;     */
+/* stream = row0 + row).                                                                       */
+/* ------------------------------------------------------------------------------------------ */
+int va_gen_gaussian(va_context* ctx, float* out, int64_t rows, int dim, uint64_t seed, int64_t row0);
+int va_gen_mixture(va_context* ctx, float* out, int64_t rows, int dim, uint64_t seed, int64_t row0,
+                   int n_centroids, float sigma, int normalize);
+/* fp32 -> bf16 (round to nearest even). */
+int va_f32_to_bf16(va_context* ctx, const float* x, int64_t n, uint16_t* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* VA_CUDA_H */

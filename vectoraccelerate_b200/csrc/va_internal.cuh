@@ -1,0 +1,242 @@
+// va_internal.cuh -- shared host/device helpers of libva_cuda (not part of the public ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/va_cuda.h"
+
+// ------------------------------------------------------------------------------------------------
+// Host-side error plumbing: every ABI function returns a status and records a thread-local message.
+// ------------------------------------------------------------------------------------------------
+int va_set_error(int code, const char* fmt, ...);
+
+#define VA_CUDA_TRY(expr)                                                                          \
+    do {                                                                                           \
+        cudaError_t _e = (expr);                                                                   \
+        if (_e != cudaSuccess)                                                                     \
+            return va_set_error(_e == cudaErrorMemoryAllocation ? VA_ERR_OOM : VA_ERR_CUDA,        \
+                                "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__,  \
+                                __LINE__);                                                         \
+    } while (0)
+
+#define VA_TRY(expr)                 \
+    do {                             \
+        int _s = (expr);             \
+        if (_s != VA_OK) return _s;  \
+    } while (0)
+
+#define VA_REQUIRE(cond, ...)                                       \
+    do {                                                            \
+        if (!(cond)) return va_set_error(VA_ERR_INVALID_ARG, __VA_ARGS__); \
+    } while (0)
+
+// Device-side error codes written to the context's error word.
+#define VA_DEVERR_WAIT_TIMEOUT 1
+
+struct va_context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    unsigned timeout_ms = 120000;
+    int sm_count = 148;
+    int* d_error = nullptr;  // device error word (bounded waits write it)
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr, ev_sync = nullptr;
+    cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr;  // bracket the dominant kernel of the last search
+    bool k_recorded = false;
+    // Optional per-call profile: event pairs around the dominant kernel of each search.
+    cudaEvent_t* prof_ev = nullptr;  // 2 * prof_cap events
+    int prof_cap = 0, prof_n = 0;
+    float last_ms = 0.f;
+    // Scratch cache: one growing device allocation reused in stream order.
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    // Staging for the host-buffer entry points (queries in, results out).
+    void* io = nullptr;
+    size_t io_bytes = 0;
+};
+
+// Device staging buffer of at least `bytes` for host-buffer calls.
+int va_io_buffer(va_context* ctx, size_t bytes, void** out);
+
+// Returns a device scratch pointer of at least `bytes` (stream-ordered reuse across calls).
+int va_workspace(va_context* ctx, size_t bytes, void** out);
+// Launch-error check right after a kernel launch.
+int va_check_launch(const char* what);
+
+struct va_database {
+    va_context* ctx = nullptr;
+    int64_t n = 0;
+    int dim = 0;
+    int dtype = VA_DTYPE_F32;
+    uint32_t id_base = 0;
+    void* rows = nullptr;        // original rows [n x dim] (fp32 or bf16)
+    uint16_t* op = nullptr;      // bf16 tensor-core operand [n x dpad], zero padded (lazily built)
+    uint16_t* op_cos = nullptr;  // bf16 unit-norm operand for cosine [n x dpad] (lazily built)
+    float* op_f32 = nullptr;     // fp32 operand for tf32 [n x dpad] (lazily built)
+    float* op_f32_cos = nullptr; // fp32 unit-norm operand for tf32 cosine (lazily built)
+    float* norms2 = nullptr;     // |x|^2 fp32 per row (fp64 accumulated), padded to 256 rows
+    int dpad = 0;                // dim rounded up to the tensor-core K block (64)
+    bool op_alias = false;       // op aliases rows (bf16 rows with dim % 64 == 0)
+    bool op_f32_alias = false;   // op_f32 aliases rows (fp32 rows with dim % 64 == 0)
+};
+
+// ------------------------------------------------------------------------------------------------
+// Device helpers
+// ------------------------------------------------------------------------------------------------
+namespace va {
+
+constexpr uint32_t kInvalidId = 0xFFFFFFFFu;
+
+// Monotone map float -> uint32 (ascending floats give ascending keys); NaN maps to the worst key.
+__device__ __forceinline__ uint32_t f2key(float v) {
+    uint32_t u = __float_as_uint(v);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0xFFFFFFFFu;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+// Key in selection order for a value under mode (0 = min, 1 = max).
+__device__ __forceinline__ uint32_t mode_key(float v, int mode) {
+    uint32_t k = f2key(v);
+    if (k == 0xFFFFFFFFu) return k;  // NaN is worst in both modes
+    return mode ? ~k : k;
+}
+__device__ __forceinline__ float mode_val(uint32_t k, int mode) { return mode ? key2f(~k) : key2f(k); }
+
+__device__ __forceinline__ uint64_t composite(uint32_t key, uint32_t id) {
+    return ((uint64_t)key << 32) | (uint64_t)id;
+}
+
+// In-place ascending bitonic sort of n (power of two) uint64 values in shared memory.
+__device__ __forceinline__ void block_bitonic_sort(uint64_t* s, int n) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < (n >> 1); i += blockDim.x) {
+                int lo = 2 * i - (i & (stride - 1));
+                int hi = lo + stride;
+                bool up = ((lo & size) == 0);
+                uint64_t a = s[lo], b = s[hi];
+                if ((a > b) == up) {
+                    s[lo] = b;
+                    s[hi] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__host__ __device__ __forceinline__ int next_pow2(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+// Shared state of block_select_radix.
+struct SelectShared {
+    unsigned hist[256];
+    unsigned long long prefix, mask;
+    int need;
+    int done;
+    int count;
+};
+
+// Block-wide exact selection of the `want` smallest 64-bit composite keys among n candidates
+// given by get(i), i < n. Composites are unique (the low 32 bits carry the id), so the
+// want-th smallest is unique and the selection has exactly min(want, n) elements. They are
+// written unsorted to out[0 .. min(want,n)). Radix passes of 8 bits from the top; a pass stops
+// early once every element with the current prefix is needed.
+template <class Get>
+__device__ int block_select_radix(int64_t n, int want, Get get, uint64_t* out, SelectShared& sh) {
+    if (n <= want) {
+        if (threadIdx.x == 0) sh.count = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = get(i);
+        __syncthreads();
+        return (int)n;
+    }
+    if (threadIdx.x == 0) {
+        sh.prefix = 0;
+        sh.mask = 0;
+        sh.need = want;
+        sh.done = 0;
+        sh.count = 0;
+    }
+    __syncthreads();
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int b = threadIdx.x; b < 256; b += blockDim.x) sh.hist[b] = 0;
+        __syncthreads();
+        const unsigned long long prefix = sh.prefix, mask = sh.mask;
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+            uint64_t c = get(i);
+            if ((c & mask) == prefix) atomicAdd(&sh.hist[(c >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            // Warp 0 finds the digit where the running count reaches `need`.
+            const int lane = threadIdx.x;
+            unsigned local[8];
+            unsigned tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                local[j] = sh.hist[lane * 8 + j];
+                tot += local[j];
+            }
+            unsigned incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                unsigned t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            unsigned excl = incl - tot;
+            const unsigned need = (unsigned)sh.need;
+            if (excl < need && need <= incl) {
+                unsigned run = excl;
+                int digit = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run + local[j] >= need) {
+                        digit = j;
+                        break;
+                    }
+                    run += local[j];
+                }
+                int d = lane * 8 + digit;
+                unsigned cnt = sh.hist[d];
+                sh.prefix = prefix | ((unsigned long long)d << shift);
+                sh.mask = mask | (0xFFull << shift);
+                sh.need = (int)(need - run);
+                sh.done = (cnt == need - run) ? 1 : 0;
+            }
+        }
+        __syncthreads();
+        if (sh.done) break;
+    }
+    const unsigned long long prefix = sh.prefix, mask = sh.mask;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        uint64_t c = get(i);
+        if ((c & mask) <= prefix) {
+            int slot = atomicAdd(&sh.count, 1);
+            if (slot < want) out[slot] = c;
+        }
+    }
+    __syncthreads();
+    return want;
+}
+
+// Bounded mbarrier / flag waits: the limit is measured on the global nanosecond timer.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+}  // namespace va

@@ -1,0 +1,480 @@
+// va_search.cu -- resident databases and the fused exact k-NN search.
+//
+// Replaces FusedL2TopKKernel.execute and its strategies (Kernels/Metal4/FusedL2TopKKernel.swift:
+// 367-427, 581-1090) and the batch flat search AcceleratedVectorIndex.searchBatchGPU
+// (Index/AcceleratedVectorIndex.swift:1278-1374), extended to cosine and inner product
+// (AccelerateFallback.swift:27-60; MetalComputeProvider.swift:119-217).
+//
+// Tensor-core route (BF16 / TF32):
+//   1. queries -> padded tensor-core operand (bf16 or fp32; unit-normalised for cosine)
+//   2. va_tc_filter: per (query tile, row split) the KP best approximate candidates
+//   3. k_merge_rerank: per query, exact radix selection of the KP best across splits, exact
+//      distances of those KP candidates in fp64 from the ORIGINAL rows (the reference's
+//      arithmetic: sum((q - x)^2), dot/(|q||x|) with 0 for a zero norm, dot), final sort by
+//      (distance, id) and the top k.
+// The exact rerank makes the reduced-precision pass a filter only: results equal the exact
+// search whenever the true top k lie in the KP-candidate pool (KP >= 3k by default).
+//
+// FP32 route: the reference's chunked two-pass strategy (executeChunkedTwoPass,
+// FusedL2TopKKernel.swift:765-1090) on exact fp32 SIMT distance tiles, with the device merge.
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+
+#include "va_internal.cuh"
+#include "va_tc.cuh"
+
+extern "C" int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* ids, int nlists,
+                                       int64_t list_stride, int len, int64_t nq, int k, int mode, float* out_vals,
+                                       uint32_t* out_ids);
+
+namespace {
+
+constexpr int KBLOCK = 64;  // tensor-core K granularity of the padded operands (elements)
+
+__device__ __forceinline__ float load_row(const void* rows, int dtype, int64_t idx) {
+    if (dtype == VA_DTYPE_BF16) return __uint_as_float((uint32_t)((const uint16_t*)rows)[idx] << 16);
+    return ((const float*)rows)[idx];
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// |x|^2 per row, fp64 accumulation rounded once; pad rows get 0. One warp per row.
+__global__ void k_norms2(const void* rows, int dtype, int64_t n, int64_t n_pad, int dim, float* out) {
+    int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (r >= n_pad) return;
+    double s = 0;
+    if (r < n)
+        for (int j = lane; j < dim; j += 32) {
+            double v = load_row(rows, dtype, r * dim + j);
+            s += v * v;
+        }
+    s = warp_sum_d(s);
+    if (lane == 0) out[r] = (float)s;
+}
+
+// Padded tensor-core operand of rows [0, n_valid) of src (rows beyond n_valid up to n_out are
+// zero). OUT = uint16_t (bf16) or float. normalize: scale each row to unit L2 norm (fp64 norm;
+// zero rows stay zero). One warp per row.
+template <class OUT>
+__global__ void k_operand(const void* src, int dtype, int64_t n_valid, int64_t n_out, int dim, int dpad,
+                          int normalize, OUT* out) {
+    int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (r >= n_out) return;
+    double scale = 1.0;
+    if (normalize && r < n_valid) {
+        double s = 0;
+        for (int j = lane; j < dim; j += 32) {
+            double v = load_row(src, dtype, r * dim + j);
+            s += v * v;
+        }
+        s = warp_sum_d(s);
+        scale = s > 0 ? 1.0 / sqrt(s) : 0.0;
+    }
+    OUT* o = out + r * dpad;
+    for (int j = lane; j < dpad; j += 32) {
+        float v = 0.f;
+        if (r < n_valid && j < dim) v = (float)(load_row(src, dtype, r * dim + j) * scale);
+        if constexpr (sizeof(OUT) == 2)
+            o[j] = f2bf(v);
+        else
+            o[j] = v;
+    }
+}
+
+// Per query: select the KP best approximate candidates over all splits, rerank exactly from the
+// original rows, emit the top k sorted by (distance, id).
+constexpr int MR_THREADS = 256;
+
+__global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
+                                                           const uint32_t* __restrict__ part_ids, int splits,
+                                                           int64_t nq_pad, int kp, const float* __restrict__ queries,
+                                                           const void* __restrict__ rows, int dtype, int dim, int metric,
+                                                           int k, uint32_t id_base, float* __restrict__ out_vals,
+                                                           uint32_t* __restrict__ out_ids) {
+    extern __shared__ uint8_t smem[];
+    const int kp2 = va::next_pow2(kp);
+    uint64_t* sel = (uint64_t*)smem;       // [kp2]
+    uint64_t* ex = sel + kp2;               // [kp2]
+    float* sq = (float*)(ex + kp2);         // [dim]
+    __shared__ va::SelectShared sh;
+    __shared__ double s_qn;
+    const int64_t qi = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+
+    for (int j = threadIdx.x; j < dim; j += blockDim.x) sq[j] = queries[qi * dim + j];
+    auto get = [&](int64_t i) -> uint64_t {
+        const int s = (int)(i / kp), j = (int)(i - (int64_t)s * kp);
+        const int64_t off = ((int64_t)s * nq_pad + qi) * kp + j;
+        const uint32_t id = part_ids[off];
+        if (id == va::kInvalidId) return ~0ull;
+        return va::composite(va::f2key(part_keys[off]), id);
+    };
+    const int m = va::block_select_radix((int64_t)splits * kp, kp, get, sel, sh);
+    if (metric == VA_METRIC_COSINE && warp == 0) {
+        double s = 0;
+        for (int j = lane; j < dim; j += 32) s += (double)sq[j] * sq[j];
+        s = warp_sum_d(s);
+        if (lane == 0) s_qn = sqrt(s);
+    }
+    __syncthreads();
+    const int mode = metric == VA_METRIC_IP ? 1 : 0;
+    for (int c = warp; c < kp2; c += nwarps) {
+        uint64_t comp = c < m ? sel[c] : ~0ull;
+        uint32_t id = (uint32_t)comp;
+        if (comp == ~0ull || id == va::kInvalidId) {
+            if (lane == 0) ex[c] = ~0ull;
+            continue;
+        }
+        const int64_t base = (int64_t)id * dim;
+        double s = 0, xx = 0;
+        if (metric == VA_METRIC_L2SQ) {
+            for (int j = lane; j < dim; j += 32) {
+                double t = (double)sq[j] - (double)load_row(rows, dtype, base + j);
+                s += t * t;
+            }
+        } else {
+            for (int j = lane; j < dim; j += 32) {
+                double xv = load_row(rows, dtype, base + j);
+                s += (double)sq[j] * xv;
+                xx += xv * xv;
+            }
+            if (metric == VA_METRIC_COSINE) xx = warp_sum_d(xx);
+        }
+        s = warp_sum_d(s);
+        if (lane == 0) {
+            float v;
+            if (metric == VA_METRIC_L2SQ || metric == VA_METRIC_IP) {
+                v = (float)s;
+            } else {
+                double den = s_qn * sqrt(xx);
+                double sim = den > 0 ? s / den : 0.0;
+                sim = fmin(1.0, fmax(-1.0, sim));
+                v = (float)(1.0 - sim);
+            }
+            ex[c] = va::composite(va::mode_key(v, mode), id);
+        }
+    }
+    va::block_bitonic_sort(ex, kp2);
+    const float pad = mode ? -INFINITY : INFINITY;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        uint64_t comp = i < kp2 ? ex[i] : ~0ull;
+        float v = pad;
+        uint32_t id = va::kInvalidId;
+        if (comp != ~0ull) {
+            id = (uint32_t)comp + id_base;
+            v = va::mode_val((uint32_t)(comp >> 32), mode);
+        }
+        out_vals[qi * k + i] = v;
+        out_ids[qi * k + i] = id;
+    }
+}
+
+__global__ void k_add_base(uint32_t* ids, int64_t n, uint32_t base) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        if (ids[i] != va::kInvalidId) ids[i] += base;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int warps_grid(int64_t warps) { return (int)((warps * 32 + 255) / 256); }
+
+// Build (once) the operand a precision/metric needs.
+int ensure_operand(va_context* ctx, va_database* db, int elem, bool cosine, const void** out) {
+    const int64_t n = db->n;
+    if (elem == 2) {
+        uint16_t** slot = cosine ? &db->op_cos : &db->op;
+        if (!*slot) {
+            if (!cosine && db->dtype == VA_DTYPE_BF16 && db->dim % KBLOCK == 0) {
+                db->op = (uint16_t*)db->rows;
+                db->op_alias = true;
+            } else {
+                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)n * db->dpad * 2));
+                k_operand<uint16_t><<<warps_grid(n), 256, 0, ctx->stream>>>(db->rows, db->dtype, n, n, db->dim,
+                                                                            db->dpad, cosine ? 1 : 0, *slot);
+                VA_TRY(va_check_launch("k_operand<bf16>"));
+            }
+        }
+        *out = *slot;
+    } else {
+        float** slot = cosine ? &db->op_f32_cos : &db->op_f32;
+        if (!*slot) {
+            if (!cosine && db->dtype == VA_DTYPE_F32 && db->dim % KBLOCK == 0) {
+                db->op_f32 = (float*)db->rows;
+                db->op_f32_alias = true;
+            } else {
+                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)n * db->dpad * 4));
+                k_operand<float><<<warps_grid(n), 256, 0, ctx->stream>>>(db->rows, db->dtype, n, n, db->dim,
+                                                                         db->dpad, cosine ? 1 : 0, *slot);
+                VA_TRY(va_check_launch("k_operand<f32>"));
+            }
+        }
+        *out = *slot;
+    }
+    return VA_OK;
+}
+
+int choose_kp(int k, int rerank) {
+    int want = rerank > 0 ? rerank * k : 3 * k;
+    if (want < k) want = k;
+    if (want <= 32) return 32;
+    if (want <= 64) return 64;
+    return 0;
+}
+
+int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
+                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, float* out_vals,
+                 uint32_t* out_ids);
+
+int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
+              int kp, float* out_vals, uint32_t* out_ids) {
+    TcPlan plan;
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    const bool cosine = metric == VA_METRIC_COSINE;
+    const void* x_op = nullptr;
+    VA_TRY(ensure_operand(ctx, db, elem, cosine, &x_op));
+    // Scratch: query operand, partial lists.
+    const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
+    const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
+    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + 256;
+    void* ws;
+    VA_TRY(va_workspace(ctx, bytes, &ws));
+    uint8_t* p = (uint8_t*)ws;
+    void* q_op = p;
+    p += round_up((int64_t)q_bytes, 256);
+    float* part_keys = (float*)p;
+    uint32_t* part_ids = (uint32_t*)(part_keys + part);
+    if (elem == 2)
+        k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
+            queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
+    else
+        k_operand<float><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
+            queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
+    VA_TRY(va_check_launch("k_operand(queries)"));
+
+    TcFilterArgs a;
+    a.q_op = q_op;
+    a.x_op = x_op;
+    a.elem_bytes = elem;
+    a.dpad = db->dpad;
+    a.n_rows = db->n;
+    a.norms2 = db->norms2;
+    a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
+    a.use_norms = metric == VA_METRIC_L2SQ ? 1 : 0;
+    a.part_keys = part_keys;
+    a.part_ids = part_ids;
+    // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
+    a.limit_ms = 2000u;
+    const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+    VA_TRY(va_tc_filter(ctx, a, plan));
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+    if (prof)
+        ctx->prof_n++;
+    else
+        ctx->k_recorded = true;
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, out_vals, out_ids);
+}
+
+int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
+                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, float* out_vals,
+                 uint32_t* out_ids) {
+    const int kp2 = va::next_pow2(plan.kp);
+    size_t smem = (size_t)kp2 * 16 + (size_t)db->dim * 4;
+    if (smem > 48 * 1024)
+        VA_CUDA_TRY(cudaFuncSetAttribute(k_merge_rerank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
+                                                                    plan.kp, queries, db->rows, db->dtype, db->dim,
+                                                                    metric, k, db->id_base, out_vals, out_ids);
+    return va_check_launch("k_merge_rerank");
+}
+
+int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, float* out_vals,
+                uint32_t* out_ids) {
+    if (db->dtype != VA_DTYPE_F32)
+        return va_set_error(VA_ERR_UNSUPPORTED, "precision FP32 needs an fp32 database (this one is bf16)");
+    const int mode = metric == VA_METRIC_IP ? VA_SELECT_MAX : VA_SELECT_MIN;
+    const int flag = metric == VA_METRIC_COSINE ? 1 : 0;
+    int64_t chunk = std::max<int64_t>(256, (int64_t)(256ll << 20) / (4 * std::max<int64_t>(nq, 1)));
+    chunk = std::min<int64_t>(chunk, db->n);
+    const size_t mat = (size_t)nq * chunk;
+    const size_t lists = (size_t)nq * k;
+    void* ws;
+    VA_TRY(va_workspace(ctx, mat * 4 + lists * 8 + 512, &ws));
+    float* dmat = (float*)ws;
+    float* cv = dmat + mat;
+    uint32_t* ci = (uint32_t*)(cv + lists);
+    const float* rows = (const float*)db->rows;
+    for (int64_t c0 = 0; c0 < db->n; c0 += chunk) {
+        const int64_t cn = std::min<int64_t>(chunk, db->n - c0);
+        VA_TRY(va_distance_matrix(ctx, queries, nq, rows + c0 * db->dim, cn, db->dim, metric, flag, dmat, cn));
+        if (c0 == 0) {
+            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, out_vals, out_ids, k));
+        } else {
+            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, cv, ci, k));
+            VA_TRY(va_topk_merge(ctx, out_vals, out_ids, k, cv, ci, k, (uint32_t)c0, nq, mode, out_vals, out_ids));
+        }
+    }
+    if (db->id_base) {
+        k_add_base<<<std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096)), 256, 0, ctx->stream>>>(
+            out_ids, nq * k, db->id_base);
+        VA_TRY(va_check_launch("k_add_base"));
+    }
+    return VA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype, uint32_t id_base,
+                 va_database** out) {
+    VA_REQUIRE(ctx && rows && out, "ctx, rows and out must not be NULL");
+    VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
+    VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
+    VA_REQUIRE(dim <= VA_MAX_DIM, "dimension %d exceeds maximum supported dimension %d", dim, VA_MAX_DIM);
+    VA_REQUIRE(dtype == VA_DTYPE_F32 || dtype == VA_DTYPE_BF16, "dtype must be VA_DTYPE_F32 or VA_DTYPE_BF16, got %d",
+               dtype);
+    VA_REQUIRE((uint64_t)n + id_base <= 0xFFFFFFFFull, "numDataset %lld + id_base %u exceeds the uint32 id range",
+               (long long)n, id_base);
+    *out = nullptr;
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    va_database* db = new va_database();
+    db->ctx = ctx;
+    db->n = n;
+    db->dim = dim;
+    db->dtype = dtype;
+    db->id_base = id_base;
+    db->dpad = (int)round_up(dim, KBLOCK);
+    const size_t esz = dtype == VA_DTYPE_BF16 ? 2 : 4;
+    const size_t bytes = (size_t)n * dim * esz;
+    const int64_t n_pad = round_up(n, 256);
+    cudaError_t e = cudaMalloc(&db->rows, bytes);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&db->norms2, (size_t)n_pad * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        va_db_destroy(db);
+        return va_set_error(VA_ERR_OOM, "database allocation (%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
+    }
+    e = cudaMemcpyAsync(db->rows, rows, bytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                        ctx->stream);
+    if (e != cudaSuccess) {
+        va_db_destroy(db);
+        return va_set_error(VA_ERR_CUDA, "database upload failed: %s", cudaGetErrorString(e));
+    }
+    k_norms2<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2);
+    int s = va_check_launch("k_norms2");
+    if (s == VA_OK) {
+        // The bf16 operand serves the default precision: build it now so searches only read.
+        const void* op;
+        s = ensure_operand(ctx, db, 2, false, &op);
+    }
+    if (s != VA_OK) {
+        va_db_destroy(db);
+        return s;
+    }
+    *out = db;
+    return VA_OK;
+}
+
+int va_db_destroy(va_database* db) {
+    if (!db) return VA_OK;
+    cudaSetDevice(db->ctx->device);
+    cudaStreamSynchronize(db->ctx->stream);
+    if (db->op && !db->op_alias) cudaFree(db->op);
+    if (db->op_cos) cudaFree(db->op_cos);
+    if (db->op_f32 && !db->op_f32_alias) cudaFree(db->op_f32);
+    if (db->op_f32_cos) cudaFree(db->op_f32_cos);
+    if (db->norms2) cudaFree(db->norms2);
+    if (db->rows) cudaFree(db->rows);
+    delete db;
+    return VA_OK;
+}
+
+int va_db_info(const va_database* db, int64_t* n, int* dim, int* dtype) {
+    VA_REQUIRE(db, "db must not be NULL");
+    if (n) *n = db->n;
+    if (dim) *dim = db->dim;
+    if (dtype) *dtype = db->dtype;
+    return VA_OK;
+}
+
+int va_db_rows(const va_database* db, const void** rows) {
+    VA_REQUIRE(db && rows, "db and rows must not be NULL");
+    *rows = db->rows;
+    return VA_OK;
+}
+
+int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int metric,
+                  int precision, int rerank, float* out_vals, uint32_t* out_ids) {
+    VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
+    VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
+    VA_REQUIRE(queries, "queries must not be NULL");
+    VA_REQUIRE(k > 0, "k must be positive, got %d", k);
+    VA_REQUIRE(k <= VA_MAX_K, "k %d exceeds maximum supported k %d", k, VA_MAX_K);
+    VA_REQUIRE(metric >= 0 && metric <= 2, "metric must be 0 (L2SQ), 1 (COSINE) or 2 (IP), got %d", metric);
+    VA_REQUIRE(precision >= VA_PREC_AUTO && precision <= VA_PREC_BF16, "precision must be 0..3, got %d", precision);
+    VA_REQUIRE(rerank >= 0, "rerank must be >= 0, got %d", rerank);
+    va_database* db = const_cast<va_database*>(cdb);
+    VA_REQUIRE(db->ctx->device == ctx->device, "database lives on device %d, context on device %d", db->ctx->device,
+               ctx->device);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    VA_CUDA_TRY(cudaEventRecord(ctx->ev_start, ctx->stream));
+    ctx->k_recorded = false;
+    int kp = choose_kp(k, rerank);
+    int prec = precision;
+    if (prec == VA_PREC_AUTO) prec = kp ? VA_PREC_BF16 : VA_PREC_FP32;
+    if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
+        if (!kp) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
+        prec = VA_PREC_BF16;
+    }
+    if (prec == VA_PREC_FP32) {
+        VA_TRY(search_fp32(ctx, db, queries, nq, k, metric, out_vals, out_ids));
+    } else {
+        if (!kp)
+            return va_set_error(VA_ERR_UNSUPPORTED,
+                                "candidate pool %d x k %d exceeds the tensor-core filter's 64; use precision FP32",
+                                rerank ? rerank : 3, k);
+        const int elem = prec == VA_PREC_TF32 ? 4 : 2;
+        VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, kp, out_vals, out_ids));
+    }
+    VA_CUDA_TRY(cudaEventRecord(ctx->ev_stop, ctx->stream));
+    return VA_OK;
+}
+
+int va_knn_search_host(va_context* ctx, const va_database* db, const float* queries_host, int64_t nq, int k,
+                       int metric, int precision, int rerank, float* out_vals_host, uint32_t* out_ids_host) {
+    VA_REQUIRE(ctx && db && queries_host && out_vals_host && out_ids_host, "all pointers must be non-NULL");
+    VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
+    VA_REQUIRE(k > 0, "k must be positive, got %d", k);
+    VA_REQUIRE(k <= VA_MAX_K, "k %d exceeds maximum supported k %d", k, VA_MAX_K);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    const size_t qb = (size_t)nq * db->dim * 4, rb = (size_t)nq * k * 4;
+    void* io;
+    VA_TRY(va_io_buffer(ctx, round_up((int64_t)qb, 256) + 2 * round_up((int64_t)rb, 256), &io));
+    float* dq = (float*)io;
+    float* dv = (float*)((uint8_t*)io + round_up((int64_t)qb, 256));
+    uint32_t* di = (uint32_t*)((uint8_t*)dv + round_up((int64_t)rb, 256));
+    VA_CUDA_TRY(cudaMemcpyAsync(dq, queries_host, qb, cudaMemcpyHostToDevice, ctx->stream));
+    VA_TRY(va_knn_search(ctx, db, dq, nq, k, metric, precision, rerank, dv, di));
+    VA_CUDA_TRY(cudaMemcpyAsync(out_vals_host, dv, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(out_ids_host, di, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_synchronize(ctx));
+    cudaEventElapsedTime(&ctx->last_ms, ctx->ev_start, ctx->ev_stop);
+    return VA_OK;
+}
+
+}  // extern "C"

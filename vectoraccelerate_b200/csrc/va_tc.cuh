@@ -1,0 +1,34 @@
+// va_tc.cuh -- host interface of the tensor-core candidate filter (va_tc.cu).
+#pragma once
+#include <stdint.h>
+
+struct va_context;
+
+// Work decomposition of one filter launch: (query tile of 128) x (row split) items, statically
+// strided over a persistent grid of at most one CTA per SM.
+struct TcPlan {
+    int n_qtiles;
+    int n_tiles;
+    int splits;
+    int kp;       // per-query candidate list length
+    int grid;
+    int64_t nq_pad;
+};
+
+struct TcFilterArgs {
+    const void* q_op;     // queries, [nq_pad x dpad] bf16 or fp32, zero padded
+    const void* x_op;     // rows, [n_rows x dpad] bf16 or fp32, zero padded
+    int elem_bytes;       // 2 = bf16 (kind::f16), 4 = fp32 read as tf32 (kind::tf32)
+    int64_t dpad;         // padded row length in elements (multiple of 64)
+    int64_t n_rows;
+    const float* norms2;  // |x|^2 per row, padded to a multiple of 256 entries (L2 only)
+    float alpha;          // key = alpha * dot + (use_norms ? norms2 : 0)
+    int use_norms;
+    float* part_keys;     // [splits][nq_pad][kp]
+    uint32_t* part_ids;   // [splits][nq_pad][kp]
+    unsigned limit_ms;    // bound of every device-side wait
+};
+
+int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
+int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
+int va_tc_stages(int kp);
