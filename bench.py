@@ -196,7 +196,10 @@ def run_ours(a):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    stream = torch.cuda.current_stream()
+    # One explicit stream shared by the library, torch copies and NCCL (the legacy default
+    # stream would make the library create its own, unordered with the timing events).
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
     ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
     prec = {"bf16": va.PREC_BF16, "tf32": va.PREC_TF32, "fp32": va.PREC_FP32}[a.precision]
 

@@ -573,15 +573,15 @@ void orc_dequantize_int8(const int8_t* in, int64_t n, float gscale, int8_t gzp, 
 }
 
 // int4 (DataTransformations.metal:224-306): q = clamp(rint(x/scale + zp), -8, 7), two codes per
-// byte, element 2i in the low nibble, 2i+1 in the high nibble.
+// byte, element 2i in the low nibble, 2i+1 in the high nibble. For an odd count the high nibble
+// of the last byte holds the code of 0.0 (the shader loads 0.0f past the end, :249).
 void orc_quantize_int4(const float* x, int64_t n, float gscale, int8_t gzp, uint8_t* out) {
-    for (int64_t i = 0; i < (n + 1) / 2; ++i) out[i] = 0;
-    for (int64_t i = 0; i < n; ++i) {
-        int q = gzp;
-        if (std::fabs(gscale) >= 1e-9f) {
-            float r = std::nearbyint(x[i] / gscale + (float)gzp);
-            q = (int)std::min(7.0f, std::max(-8.0f, r));
-        }
+    const int64_t nb = (n + 1) / 2;
+    for (int64_t i = 0; i < nb; ++i) out[i] = 0;
+    for (int64_t i = 0; i < 2 * nb; ++i) {
+        const float v = i < n ? x[i] : 0.0f;
+        float r = std::fabs(gscale) < 1e-9f ? (float)gzp : std::nearbyint(v / gscale + (float)gzp);
+        int q = (int)std::min(7.0f, std::max(-8.0f, r));
         uint8_t nib = (uint8_t)(q & 0xF);
         out[i / 2] |= (i & 1) ? (uint8_t)(nib << 4) : nib;
     }

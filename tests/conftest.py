@@ -38,9 +38,9 @@ def assert_knn_parity(gpu_ids, gpu_vals, ora_ids, ora_vals, gpu_true_vals, rel_t
     gpu_ids = np.asarray(gpu_ids)
     ora_ids = np.asarray(ora_ids)
     assert gpu_ids.shape == ora_ids.shape
-    scale = np.maximum(np.abs(ora_vals), 1e-6)
-    dist_err = np.abs(gpu_vals - ora_vals) / scale
     valid = ora_ids != 0xFFFFFFFF
+    scale = np.maximum(np.abs(np.where(valid, ora_vals, 1.0)), 1e-6)
+    dist_err = np.where(valid, np.abs(np.where(valid, gpu_vals, 0) - np.where(valid, ora_vals, 0)), 0) / scale
     assert np.all(dist_err[valid] <= rel_dist), f"max relative distance error {dist_err[valid].max():.3g}"
     assert np.array_equal(gpu_ids == 0xFFFFFFFF, ora_ids == 0xFFFFFFFF), "padding differs"
     mism = (gpu_ids != ora_ids) & valid

@@ -171,21 +171,15 @@ int va_cosine_pairs(va_context* ctx, const float* a, const float* b, int64_t pai
     return va_check_launch("k_cos_pairs");
 }
 
-int va_distance_matrix(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim, int metric,
-                       int flag, float* out, int64_t out_stride) {
-    VA_REQUIRE(ctx && q && x && out, "ctx, q, x and out must not be NULL");
-    VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
-    VA_REQUIRE(metric >= 0 && metric <= 2, "metric must be 0 (L2SQ), 1 (COSINE) or 2 (IP), got %d", metric);
-    VA_REQUIRE(nq >= 0 && nx >= 0, "nq and nx must be >= 0");
-    VA_REQUIRE(out_stride >= nx, "out_stride %lld must be >= nx %lld", (long long)out_stride, (long long)nx);
-    if (!nq || !nx) return VA_OK;
-    VA_REQUIRE((nq + TM - 1) / TM <= 65535, "nq %lld too large for one matrix call", (long long)nq);
-    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+}  // extern "C"
+
+// Matrix with caller-provided norm scratch (nq + nx floats; used for cosine only), so internal
+// callers can keep the context workspace for their own buffers.
+int va_distance_matrix_impl(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
+                            int metric, int flag, float* out, int64_t out_stride, float* norm_scratch) {
     float *qn = nullptr, *xn = nullptr;
     if (metric == VA_METRIC_COSINE) {
-        void* ws;
-        VA_TRY(va_workspace(ctx, (size_t)(nq + nx) * sizeof(float), &ws));
-        qn = (float*)ws;
+        qn = norm_scratch;
         xn = qn + nq;
         k_row_norms<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, ctx->stream>>>(q, nq, dim, qn);
         k_row_norms<<<(unsigned)((nx * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, nx, dim, xn);
@@ -197,6 +191,23 @@ int va_distance_matrix(va_context* ctx, const float* q, int64_t nq, const float*
     else
         k_matrix<1><<<grid, 256, 0, ctx->stream>>>(q, nq, x, nx, dim, metric, flag, qn, xn, out, out_stride);
     return va_check_launch("k_matrix");
+}
+
+extern "C" {
+
+int va_distance_matrix(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim, int metric,
+                       int flag, float* out, int64_t out_stride) {
+    VA_REQUIRE(ctx && q && x && out, "ctx, q, x and out must not be NULL");
+    VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
+    VA_REQUIRE(metric >= 0 && metric <= 2, "metric must be 0 (L2SQ), 1 (COSINE) or 2 (IP), got %d", metric);
+    VA_REQUIRE(nq >= 0 && nx >= 0, "nq and nx must be >= 0");
+    VA_REQUIRE(out_stride >= nx, "out_stride %lld must be >= nx %lld", (long long)out_stride, (long long)nx);
+    if (!nq || !nx) return VA_OK;
+    VA_REQUIRE((nq + TM - 1) / TM <= 65535, "nq %lld too large for one matrix call", (long long)nq);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    void* ws = nullptr;
+    if (metric == VA_METRIC_COSINE) VA_TRY(va_workspace(ctx, (size_t)(nq + nx) * sizeof(float), &ws));
+    return va_distance_matrix_impl(ctx, q, nq, x, nx, dim, metric, flag, out, out_stride, (float*)ws);
 }
 
 }  // extern "C"

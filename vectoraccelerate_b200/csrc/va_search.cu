@@ -24,6 +24,9 @@
 #include "va_internal.cuh"
 #include "va_tc.cuh"
 
+int va_distance_matrix_impl(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
+                            int metric, int flag, float* out, int64_t out_stride, float* norm_scratch);
+
 extern "C" int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* ids, int nlists,
                                        int64_t list_stride, int len, int64_t nq, int k, int mode, float* out_vals,
                                        uint32_t* out_ids);
@@ -312,15 +315,19 @@ int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t 
     chunk = std::min<int64_t>(chunk, db->n);
     const size_t mat = (size_t)nq * chunk;
     const size_t lists = (size_t)nq * k;
+    const size_t norms = (size_t)nq + chunk;
     void* ws;
-    VA_TRY(va_workspace(ctx, mat * 4 + lists * 8 + 512, &ws));
+    VA_TRY(va_workspace(ctx, (mat + norms) * 4 + lists * 8 + 512, &ws));
     float* dmat = (float*)ws;
     float* cv = dmat + mat;
     uint32_t* ci = (uint32_t*)(cv + lists);
+    float* nscratch = (float*)(ci + lists);
     const float* rows = (const float*)db->rows;
     for (int64_t c0 = 0; c0 < db->n; c0 += chunk) {
         const int64_t cn = std::min<int64_t>(chunk, db->n - c0);
-        VA_TRY(va_distance_matrix(ctx, queries, nq, rows + c0 * db->dim, cn, db->dim, metric, flag, dmat, cn));
+        VA_REQUIRE((nq + 63) / 64 <= 65535, "numQueries %lld too large for the FP32 route", (long long)nq);
+        VA_TRY(va_distance_matrix_impl(ctx, queries, nq, rows + c0 * db->dim, cn, db->dim, metric, flag, dmat, cn,
+                                       nscratch));
         if (c0 == 0) {
             VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, out_vals, out_ids, k));
         } else {
