@@ -79,7 +79,8 @@ struct va_database {
     uint16_t* op_cos = nullptr;  // bf16 unit-norm operand for cosine [n x dpad] (lazily built)
     float* op_f32 = nullptr;     // fp32 operand for tf32 [n x dpad] (lazily built)
     float* op_f32_cos = nullptr; // fp32 unit-norm operand for tf32 cosine (lazily built)
-    float* norms2 = nullptr;     // |x|^2 fp32 per row (fp64 accumulated), padded to 256 rows
+    float* norms2 = nullptr;     // |x|^2 fp32 per row (fp64 accumulated); +inf pad to 256 rows
+    float* zbias = nullptr;      // 0 per row; +inf pad to 256 rows (filter bias of IP / cosine)
     int dpad = 0;                // dim rounded up to the tensor-core K block (64)
     bool op_alias = false;       // op aliases rows (bf16 rows with dim % 64 == 0)
     bool op_f32_alias = false;   // op_f32 aliases rows (fp32 rows with dim % 64 == 0)

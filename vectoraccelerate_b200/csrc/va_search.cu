@@ -53,8 +53,11 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
     return (uint16_t)(u >> 16);
 }
 
-// |x|^2 per row, fp64 accumulation rounded once; pad rows get 0. One warp per row.
-__global__ void k_norms2(const void* rows, int dtype, int64_t n, int64_t n_pad, int dim, float* out) {
+// Filter row biases: norms2[r] = |x_r|^2 (fp64 accumulation rounded once) and zbias[r] = 0 for
+// real rows; both +inf for the pad rows up to n_pad so padded tile columns never pass the
+// filter. One warp per row.
+__global__ void k_row_bias(const void* rows, int dtype, int64_t n, int64_t n_pad, int dim, float* norms2,
+                           float* zbias) {
     int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (r >= n_pad) return;
@@ -65,7 +68,10 @@ __global__ void k_norms2(const void* rows, int dtype, int64_t n, int64_t n_pad, 
             s += v * v;
         }
     s = warp_sum_d(s);
-    if (lane == 0) out[r] = (float)s;
+    if (lane == 0) {
+        norms2[r] = r < n ? (float)s : INFINITY;
+        zbias[r] = r < n ? 0.f : INFINITY;
+    }
 }
 
 // Padded tensor-core operand of rows [0, n_valid) of src (rows beyond n_valid up to n_out are
@@ -249,10 +255,10 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = nullptr;
     VA_TRY(ensure_operand(ctx, db, elem, cosine, &x_op));
-    // Scratch: query operand, partial lists.
+    // Scratch: query operand, partial lists, shared per-query bounds.
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
-    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + 256;
+    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + 256;
     void* ws;
     VA_TRY(va_workspace(ctx, bytes, &ws));
     uint8_t* p = (uint8_t*)ws;
@@ -260,6 +266,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     p += round_up((int64_t)q_bytes, 256);
     float* part_keys = (float*)p;
     uint32_t* part_ids = (uint32_t*)(part_keys + part);
+    uint32_t* gthr = part_ids + part;
     if (elem == 2)
         k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
@@ -274,11 +281,11 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     a.elem_bytes = elem;
     a.dpad = db->dpad;
     a.n_rows = db->n;
-    a.norms2 = db->norms2;
+    a.row_bias = metric == VA_METRIC_L2SQ ? db->norms2 : db->zbias;
     a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
-    a.use_norms = metric == VA_METRIC_L2SQ ? 1 : 0;
     a.part_keys = part_keys;
     a.part_ids = part_ids;
+    a.gthr = gthr;
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
     const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
@@ -371,6 +378,7 @@ int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, in
     const int64_t n_pad = round_up(n, 256);
     cudaError_t e = cudaMalloc(&db->rows, bytes);
     if (e == cudaSuccess) e = cudaMalloc((void**)&db->norms2, (size_t)n_pad * 4);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&db->zbias, (size_t)n_pad * 4);
     if (e != cudaSuccess) {
         cudaGetLastError();
         va_db_destroy(db);
@@ -382,8 +390,8 @@ int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, in
         va_db_destroy(db);
         return va_set_error(VA_ERR_CUDA, "database upload failed: %s", cudaGetErrorString(e));
     }
-    k_norms2<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2);
-    int s = va_check_launch("k_norms2");
+    k_row_bias<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2, db->zbias);
+    int s = va_check_launch("k_row_bias");
     if (s == VA_OK) {
         // The bf16 operand serves the default precision: build it now so searches only read.
         const void* op;
@@ -406,6 +414,7 @@ int va_db_destroy(va_database* db) {
     if (db->op_f32 && !db->op_f32_alias) cudaFree(db->op_f32);
     if (db->op_f32_cos) cudaFree(db->op_f32_cos);
     if (db->norms2) cudaFree(db->norms2);
+    if (db->zbias) cudaFree(db->zbias);
     if (db->rows) cudaFree(db->rows);
     delete db;
     return VA_OK;

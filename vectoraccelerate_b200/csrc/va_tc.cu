@@ -14,6 +14,12 @@
 //                 key = alpha * (q.x) + |x|^2 term, and keeps a per-query sorted list of the KP
 //                 best (key, id) in shared memory, touched only when a key beats the KP-th best
 //
+// Every (query tile, row split) item starts its lists empty, so without help each item would
+// re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share one bound per
+// query in global memory: a finished item publishes its KP-th key (atomicMin on the orderable
+// key); others drop keys above the smallest published bound. The bound is the KP-th key of a
+// subset of rows, never below the global KP-th key, so no candidate of the final pool is lost.
+//
 // Two accumulators let the epilogue of tile t overlap the MMAs of tile t+1. The distance
 // matrix never reaches HBM: per (query tile, row split) work item each query's KP best
 // approximate candidates are written out, merged across splits and exactly reranked in fp64
@@ -152,6 +158,38 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Insert (key, id) into the sorted list of query `row` (entries [j*BM + row], j < KP) and return
+// the list's new KP-th key. Called only when key beats the current threshold, so it is kept out
+// of line to keep the hot loop small. Candidates arrive in increasing id order: a key equal to an
+// entry goes after it, which is the (key, id) order.
+template <int KP>
+__device__ __noinline__ float list_insert(float* lk, uint32_t* li, int row, float key, uint32_t id) {
+    int p = KP - 1;
+    while (p > 0) {
+        const float prev = lk[(p - 1) * BM + row];
+        if (prev <= key) break;
+        lk[p * BM + row] = prev;
+        li[p * BM + row] = li[(p - 1) * BM + row];
+        --p;
+    }
+    lk[p * BM + row] = key;
+    li[p * BM + row] = id;
+    return lk[(KP - 1) * BM + row];
+}
+
+// Smallest float strictly above v (v finite or +inf).
+__device__ __forceinline__ float next_up(float v) {
+    if (v == INFINITY) return v;
+    return nextafterf(v, INFINITY);
+}
+
+// Filter bound from the shared per-query key (0xFFFFFFFF = nothing published yet): the next
+// float above the published key, so keys equal to it still pass.
+__device__ __forceinline__ float load_bound(const uint32_t* g) {
+    const uint32_t k = __ldcg(g);
+    return k == 0xFFFFFFFFu ? INFINITY : next_up(va::key2f(k));
+}
+
 struct Work {
     int n_qtiles;
     int splits;
@@ -171,8 +209,9 @@ __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int
 template <int ELEM, int KP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_tc_filter(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, Work w,
-                const float* __restrict__ norms2, float alpha, int use_norms, float* __restrict__ part_keys,
-                uint32_t* __restrict__ part_ids, int* err, uint64_t limit_ns, int stages) {
+                const float* __restrict__ row_bias, float alpha, float* __restrict__ part_keys,
+                uint32_t* __restrict__ part_ids, uint32_t* __restrict__ gthr, int* err, uint64_t limit_ns,
+                int stages) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the 128B-swizzled operand slots.
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -270,18 +309,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue (warps 2..5)
+        // Thresholds: thr_own = this item's KP-th best key; thr_g = the smallest KP-th key any
+        // finished item published for this query (an upper bound of the global KP-th key, so a
+        // key above it can never reach the final pool). A candidate is inserted when
+        // key < min(thr_own, next_up(thr_g)).
         const int quarter = warp & 3;             // TMEM lane quarter this warp may access
         const int row = quarter * 32 + lane;      // query row within the tile
         uint32_t tile = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             int qt, t0, t1;
             item_range(w, item, qt, t0, t1);
+            const int64_t q = (int64_t)qt * BM + row;
             for (int j = 0; j < KP; ++j) {
                 l_key[j * BM + row] = INFINITY;
                 l_id[j * BM + row] = va::kInvalidId;
             }
-            float thr = INFINITY;
+            float thr_own = INFINITY;
+            float thr_g = load_bound(gthr + q);
+            float thr = thr_g;
             for (int t = t0; t < t1; ++t, ++tile) {
+                if (((t - t0) & 7) == 7) {
+                    thr_g = load_bound(gthr + q);
+                    thr = fminf(thr_own, thr_g);
+                }
                 const uint32_t buf = tile & 1u;
                 const uint32_t tph = (tile >> 1) & 1u;
                 // One lane waits; the warp follows its verdict so tcgen05.ld stays warp-uniform.
@@ -292,41 +342,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
                 const int64_t col0 = (int64_t)t * BN;
+                // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row)
+                // live 8 per lane and are broadcast by shuffles.
+                const float4* bp = (const float4*)(row_bias + col0) + lane * 2;
+                const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+                const float bias[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) {
                     __syncwarp();
                     float v[32];
                     tmem_ld32(taddr + c * 32, v);
-                    const int64_t cb = col0 + c * 32;
-                    float nrm[32];
-                    if (use_norms) {
-                        const float4* np = (const float4*)(norms2 + cb);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            float4 f = __ldg(np + i);
-                            nrm[4 * i] = f.x;
-                            nrm[4 * i + 1] = f.y;
-                            nrm[4 * i + 2] = f.z;
-                            nrm[4 * i + 3] = f.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) nrm[i] = 0.f;
-                    }
+                    const uint32_t cb = (uint32_t)(col0 + c * 32);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const float key = fmaf(alpha, v[i], nrm[i]);
-                        if (key < thr && cb + i < w.n_rows) {
-                            const uint32_t id = (uint32_t)(cb + i);
-                            int p = KP - 1;
-                            while (p > 0 && l_key[(p - 1) * BM + row] > key) {
-                                l_key[p * BM + row] = l_key[(p - 1) * BM + row];
-                                l_id[p * BM + row] = l_id[(p - 1) * BM + row];
-                                --p;
-                            }
-                            l_key[p * BM + row] = key;
-                            l_id[p * BM + row] = id;
-                            thr = l_key[(KP - 1) * BM + row];
+                        const float nb = __shfl_sync(0xFFFFFFFFu, bias[i & 7], c * 4 + (i >> 3));
+                        const float key = fmaf(alpha, v[i], nb);
+                        if (key < thr) {
+                            thr_own = list_insert<KP>(l_key, l_id, row, key, cb + i);
+                            thr = fminf(thr_own, thr_g);
                         }
                     }
                 }
@@ -335,8 +368,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
             {
+                // Publish this item's KP-th key (finite once the list is full) as a bound.
+                if (thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
                 const int s = item / w.n_qtiles;
-                const int64_t q = (int64_t)qt * BM + row;
                 float* pk = part_keys + ((int64_t)s * w.nq_pad + q) * KP;
                 uint32_t* pi = part_ids + ((int64_t)s * w.nq_pad + q) * KP;
 #pragma unroll 4
@@ -391,9 +425,9 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
                   const CUtensorMap& mx, const Work& w, int grid) {
     auto kern = k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<grid, NUM_THREADS, smem, ctx->stream>>>(mq, mx, w, a.norms2, a.alpha, a.use_norms, a.part_keys,
-                                                   a.part_ids, ctx->d_error, (uint64_t)a.limit_ms * 1000000ull,
-                                                   stages);
+    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nq_pad * sizeof(uint32_t), ctx->stream));
+    kern<<<grid, NUM_THREADS, smem, ctx->stream>>>(mq, mx, w, a.row_bias, a.alpha, a.part_keys, a.part_ids, a.gthr,
+                                                   ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages);
     return va_check_launch("k_tc_filter");
 }
 

@@ -21,11 +21,12 @@ struct TcFilterArgs {
     int elem_bytes;       // 2 = bf16 (kind::f16), 4 = fp32 read as tf32 (kind::tf32)
     int64_t dpad;         // padded row length in elements (multiple of 64)
     int64_t n_rows;
-    const float* norms2;  // |x|^2 per row, padded to a multiple of 256 entries (L2 only)
-    float alpha;          // key = alpha * dot + (use_norms ? norms2 : 0)
-    int use_norms;
-    float* part_keys;     // [splits][nq_pad][kp]
-    uint32_t* part_ids;   // [splits][nq_pad][kp]
+    const float* row_bias;  // per row: |x|^2 (L2) or 0 (IP, cosine); +inf for the rows past n_rows
+                            // up to a multiple of 256 (those never pass the filter)
+    float alpha;            // key = alpha * dot + row_bias
+    float* part_keys;       // [splits][nq_pad][kp]
+    uint32_t* part_ids;     // [splits][nq_pad][kp]
+    uint32_t* gthr;         // [nq_pad] shared per-query bound (orderable key), set to 0xFF bytes
     unsigned limit_ms;    // bound of every device-side wait
 };
 
