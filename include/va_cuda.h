@@ -195,6 +195,25 @@ int va_knn_search(va_context* ctx, const va_database* db, const float* queries, 
 int va_knn_search_host(va_context* ctx, const va_database* db, const float* queries_host, int64_t nq, int k,
                        int metric, int precision, int rerank, float* out_vals_host, uint32_t* out_ids_host);
 
+/* Size of the fixed device scratch of va_knn_search_noalloc (16 MiB per GPU). */
+#define VA_NOALLOC_SCRATCH_BYTES (16u << 20)
+/* va_knn_search without any device allocation; this entry point has no counterpart in the
+ * reference. For callers that must not allocate at search time: processes that give all free
+ * device memory to their own pool at start-up, callers whose device memory belongs to another
+ * allocator, and latency-bound paths that cannot take an allocation's implicit synchronisation.
+ * Inputs, outputs and the database are the caller's, as for va_knn_search; the search's scratch
+ * lives in one fixed device array of VA_NOALLOC_SCRATCH_BYTES that every GPU loading this
+ * library holds until exit. Limits: the tensor-core route only (precision AUTO, BF16 or TF32);
+ * batches whose scratch exceeds the array are rejected with VA_ERR_INVALID_ARG naming the bytes
+ * needed (up to 256 queries fit at any dimension <= VA_MAX_DIM with the default pool); the
+ * database must already hold the operand the metric/precision needs (bf16 for L2/IP is built by
+ * va_db_create; others by a first va_knn_search), else VA_ERR_UNSUPPORTED. The first call on a
+ * device looks up the array's device address (make it before any stream capture). Every call
+ * shares the array, so calls that overlap on the GPU (other streams or contexts of the same
+ * device) race; serialise them. */
+int va_knn_search_noalloc(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k,
+                          int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids);
+
 /* ------------------------------------------------------------------------------------------ */
 /* Scalar quantization (ScalarQuantizationKernel, Kernels/Metal4/ScalarQuantizationKernel.swift;  */
 /* quantize_int8_kernel / dequantize_int8_kernel / int4, DataTransformations.metal:142-306)      */

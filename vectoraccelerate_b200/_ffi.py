@@ -69,6 +69,7 @@ SIGNATURES = {
     "va_db_rows": [_P, _PP],
     "va_knn_search": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_knn_search_host": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
+    "va_knn_search_noalloc": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_sq_quantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_dequantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_quantize_int4": [_P, _P, _I64, _F, ctypes.c_int8, _P],

@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <mutex>
 
 #include "va_internal.cuh"
 #include "va_tc.cuh"
@@ -494,3 +495,117 @@ int va_knn_search_host(va_context* ctx, const va_database* db, const float* quer
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Search without device allocation.
+//
+// Some callers cannot let a search call cudaMalloc: serving processes that hand all free device
+// memory to their own pool at start-up (a later cudaMalloc would fail), callers whose device
+// memory is owned by another allocator that forbids side allocations, and latency-bound paths
+// where an allocation's implicit device synchronisation would stall other streams.
+// va_knn_search_noalloc gives them the tensor-core search with its scratch (query operand,
+// per-split candidate lists, per-query bounds) in one fixed device array of
+// VA_NOALLOC_SCRATCH_BYTES, declared below; every GPU that loads the library holds that array
+// until the process exits.
+// ------------------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[VA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch on each device. In host code the array's name is only a
+// host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device, with that
+// device current.
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[256] = {};
+
+int noalloc_scratch(int device, void** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device < 0 || device >= 256) return va_set_error(VA_ERR_INVALID_ARG, "device %d out of range", device);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return va_set_error(VA_ERR_CUDA, "cudaGetSymbolAddress of the fixed scratch failed on device %d: %s",
+                                device, cudaGetErrorString(e));
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return VA_OK;
+}
+
+// Same steps as search_tc, with the scratch carved from a caller-provided region.
+int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
+                    int kp, uint8_t* scratch, size_t scratch_bytes, float* out_vals, uint32_t* out_ids) {
+    TcPlan plan;
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    const bool cosine = metric == VA_METRIC_COSINE;
+    const void* x_op = elem == 2 ? (cosine ? (const void*)db->op_cos : (const void*)db->op)
+                                 : (cosine ? (const void*)db->op_f32_cos : (const void*)db->op_f32);
+    if (!x_op)
+        return va_set_error(VA_ERR_UNSUPPORTED,
+                            "the %s operand of this database is not built yet and building it would allocate; run "
+                            "one va_knn_search with this metric and precision first",
+                            elem == 2 ? (cosine ? "unit-norm bf16" : "bf16") : (cosine ? "unit-norm fp32" : "fp32"));
+    const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
+    const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
+    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4;
+    if (bytes > scratch_bytes)
+        return va_set_error(VA_ERR_INVALID_ARG,
+                            "numQueries %lld at dimension %d needs %zu bytes of scratch; the allocation-free search "
+                            "has %zu (split the batch)",
+                            (long long)nq, db->dim, bytes, scratch_bytes);
+    uint8_t* p = scratch;
+    void* q_op = p;
+    p += round_up((int64_t)q_bytes, 256);
+    float* part_keys = (float*)p;
+    uint32_t* part_ids = (uint32_t*)(part_keys + part);
+    uint32_t* gthr = part_ids + part;
+    if (elem == 2)
+        k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
+            queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
+    else
+        k_operand<float><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
+            queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
+    VA_TRY(va_check_launch("k_operand(queries)"));
+    TcFilterArgs a;
+    a.q_op = q_op;
+    a.x_op = x_op;
+    a.elem_bytes = elem;
+    a.dpad = db->dpad;
+    a.n_rows = db->n;
+    a.row_bias = metric == VA_METRIC_L2SQ ? db->norms2 : db->zbias;
+    a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
+    a.part_keys = part_keys;
+    a.part_ids = part_ids;
+    a.gthr = gthr;  // va_tc_filter resets it before the launch
+    a.limit_ms = 2000u;
+    VA_TRY(va_tc_filter(ctx, a, plan));
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, out_vals, out_ids);
+}
+
+}  // namespace
+
+extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k,
+                                     int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids) {
+    VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
+    VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
+    VA_REQUIRE(queries, "queries must not be NULL");
+    VA_REQUIRE(k > 0, "k must be positive, got %d", k);
+    VA_REQUIRE(k <= VA_MAX_K, "k %d exceeds maximum supported k %d", k, VA_MAX_K);
+    VA_REQUIRE(metric >= 0 && metric <= 2, "metric must be 0 (L2SQ), 1 (COSINE) or 2 (IP), got %d", metric);
+    VA_REQUIRE(precision == VA_PREC_AUTO || precision == VA_PREC_BF16 || precision == VA_PREC_TF32,
+               "the allocation-free search runs the tensor-core route only (precision AUTO, BF16 or TF32), got %d",
+               precision);
+    VA_REQUIRE(rerank >= 0, "rerank must be >= 0, got %d", rerank);
+    va_database* db = const_cast<va_database*>(cdb);
+    VA_REQUIRE(db->ctx->device == ctx->device, "database lives on device %d, context on device %d", db->ctx->device,
+               ctx->device);
+    const int kp = choose_kp(k, rerank);
+    VA_REQUIRE(kp > 0, "candidate pool of k %d exceeds the tensor-core filter's 64", k);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    void* scratch = nullptr;
+    VA_TRY(noalloc_scratch(ctx->device, &scratch));
+    const int elem = precision == VA_PREC_TF32 ? 4 : 2;
+    return search_tc_fixed(ctx, db, queries, nq, k, metric, elem, kp, (uint8_t*)scratch, VA_NOALLOC_SCRATCH_BYTES,
+                           out_vals, out_ids);
+}
