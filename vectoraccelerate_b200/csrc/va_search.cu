@@ -259,7 +259,8 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     // Scratch: query operand, partial lists, shared per-query bounds.
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
-    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + 256;
+    const size_t bytes =
+        round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + (size_t)plan.sync_words * 4 + 256;
     void* ws;
     VA_TRY(va_workspace(ctx, bytes, &ws));
     uint8_t* p = (uint8_t*)ws;
@@ -268,6 +269,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     float* part_keys = (float*)p;
     uint32_t* part_ids = (uint32_t*)(part_keys + part);
     uint32_t* gthr = part_ids + part;
+    uint32_t* sync_cnt = gthr + plan.nq_pad;
     if (elem == 2)
         k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
@@ -287,6 +289,8 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     a.part_keys = part_keys;
     a.part_ids = part_ids;
     a.gthr = gthr;
+    a.sync_cnt = sync_cnt;
+    a.sync_words = plan.sync_words;
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
     const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
@@ -548,7 +552,8 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
                             elem == 2 ? (cosine ? "unit-norm bf16" : "bf16") : (cosine ? "unit-norm fp32" : "fp32"));
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
-    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4;
+    const size_t bytes =
+        round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + (size_t)plan.sync_words * 4;
     if (bytes > scratch_bytes)
         return va_set_error(VA_ERR_INVALID_ARG,
                             "numQueries %lld at dimension %d needs %zu bytes of scratch; the allocation-free search "
@@ -560,6 +565,7 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
     float* part_keys = (float*)p;
     uint32_t* part_ids = (uint32_t*)(part_keys + part);
     uint32_t* gthr = part_ids + part;
+    uint32_t* sync_cnt = gthr + plan.nq_pad;
     if (elem == 2)
         k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
@@ -577,7 +583,9 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
     a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
     a.part_keys = part_keys;
     a.part_ids = part_ids;
-    a.gthr = gthr;  // va_tc_filter resets it before the launch
+    a.gthr = gthr;          // va_tc_filter resets it before the launch
+    a.sync_cnt = sync_cnt;  // likewise
+    a.sync_words = plan.sync_words;
     a.limit_ms = 2000u;
     VA_TRY(va_tc_filter(ctx, a, plan));
     return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, out_vals, out_ids);

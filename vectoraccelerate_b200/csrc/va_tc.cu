@@ -142,39 +142,146 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
-    uint32_t r[32];
+// Issue a 64-column TMEM load (one accumulator row per thread); the registers are valid only
+// after tmem_wait64 on the same array.
+__device__ __forceinline__ void tmem_ld64(uint32_t addr, uint32_t (&r)[64]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
         : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Insert (key, id) into the sorted list of query `row` (entries [j*BM + row], j < KP) and return
-// the list's new KP-th key. Called only when key beats the current threshold, so it is kept out
-// of line to keep the hot loop small. Candidates arrive in increasing id order: a key equal to an
-// entry goes after it, which is the (key, id) order.
+// Wait for every outstanding TMEM load of this thread. The array is an in/out operand so the
+// compiler cannot move any use of its registers above the wait.
+__device__ __forceinline__ void tmem_wait64(uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+          "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+          "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]),
+          "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]),
+          "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]),
+          "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]),
+          "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+        :
+        : "memory");
+}
+
+// Candidate lists live in shared memory row-contiguous: query row r owns keys lk[r*KP + j] and
+// ids li[r*KP + j], j < KP, sorted by (key, id). The 32 lanes of a warp update one row's list
+// together: lane l holds entries l, l + 32, ... (E = KP / 32 per lane).
+//
+// Insert (key, id) into row r's list (warp-uniform arguments) and return the new KP-th key.
+// The position is the number of entries <= key (candidates arrive in increasing id order, so an
+// equal key goes after the entries already there: the (key, id) order); entries from the position
+// on move up one slot with a shuffle. No loop over KP, no serial shared-memory chain.
 template <int KP>
-__device__ __noinline__ float list_insert(float* lk, uint32_t* li, int row, float key, uint32_t id) {
-    int p = KP - 1;
-    while (p > 0) {
-        const float prev = lk[(p - 1) * BM + row];
-        if (prev <= key) break;
-        lk[p * BM + row] = prev;
-        li[p * BM + row] = li[(p - 1) * BM + row];
-        --p;
+__device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r, float key, uint32_t id, int lane) {
+    constexpr int E = KP / 32;
+    float ek[E];
+    uint32_t ei[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+        ek[k] = lk[r * KP + k * 32 + lane];
+        ei[k] = li[r * KP + k * 32 + lane];
     }
-    lk[p * BM + row] = key;
-    li[p * BM + row] = id;
-    return lk[(KP - 1) * BM + row];
+    int pos = 0;
+#pragma unroll
+    for (int k = 0; k < E; ++k) pos += __popc(__ballot_sync(0xFFFFFFFFu, ek[k] <= key));
+    float last = 0.f;
+#pragma unroll
+    for (int k = E - 1; k >= 0; --k) {
+        // previous entry (position p - 1) of this lane's slot p = 32k + lane
+        float pk = __shfl_up_sync(0xFFFFFFFFu, ek[k], 1);
+        uint32_t pi = __shfl_up_sync(0xFFFFFFFFu, ei[k], 1);
+        if (k > 0) {
+            const float wk = __shfl_sync(0xFFFFFFFFu, ek[k - 1], 31);
+            const uint32_t wi = __shfl_sync(0xFFFFFFFFu, ei[k - 1], 31);
+            if (lane == 0) {
+                pk = wk;
+                pi = wi;
+            }
+        }
+        const int p = 32 * k + lane;
+        if (p >= pos) {
+            const float nk = p == pos ? key : pk;
+            const uint32_t ni = p == pos ? id : pi;
+            lk[r * KP + p] = nk;
+            li[r * KP + p] = ni;
+            if (k == E - 1) last = nk;
+        } else if (k == E - 1) {
+            last = ek[k];
+        }
+    }
+    return __shfl_sync(0xFFFFFFFFu, last, 31);
+}
+
+// One 64-column chunk C (compile-time, so every shuffle reads a fixed register of a fixed lane).
+// Fast path: key = alpha * acc + bias (bias of column 64C + i sits in lane i % 32, register
+// 2C + i / 32) kept in place in r, eight partial minima, and one warp-uniform branch. Cold path,
+// when some lane's minimum beats its threshold: each lane marks its passing columns; the warp
+// then inserts the marked candidates one at a time (lowest lane first, each lane in column
+// order), re-checking each against the owning lane's current threshold.
+template <int C, int KP>
+__device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bias)[8], float alpha, uint32_t id0,
+                                             float* lk, uint32_t* li, int row0, int lane, float thr_g,
+                                             float& thr_own, float& thr) {
+    float mn[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mn[j] = INFINITY;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+        const float b = __shfl_sync(0xFFFFFFFFu, bias[2 * C + (i >> 5)], i & 31);
+        const float key = fmaf(alpha, __uint_as_float(r[i]), b);
+        r[i] = __float_as_uint(key);
+        mn[i & 7] = fminf(mn[i & 7], key);
+    }
+    const float m = fminf(fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3])), fminf(fminf(mn[4], mn[5]), fminf(mn[6], mn[7])));
+    if (!__any_sync(0xFFFFFFFFu, m < thr)) return;
+    uint64_t pass = 0;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) pass |= (uint64_t)(__uint_as_float(r[i]) < thr) << i;
+    // Lanes with marked columns park their keys in thread-local memory for indexed reads.
+    float kk[64];
+    if (pass) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) kk[i] = __uint_as_float(r[i]);
+    }
+    for (;;) {
+        const uint32_t lanes = __ballot_sync(0xFFFFFFFFu, pass != 0);
+        if (!lanes) break;
+        const int L = __ffs(lanes) - 1;
+        // the leader's lowest marked column and its key, broadcast to the warp
+        int i = 0;
+        float key = 0.f;
+        if (lane == L) {
+            i = __ffsll((long long)pass) - 1;
+            pass &= pass - 1;
+            key = kk[i];
+        }
+        i = __shfl_sync(0xFFFFFFFFu, i, L);
+        key = __shfl_sync(0xFFFFFFFFu, key, L);
+        const float thrL = __shfl_sync(0xFFFFFFFFu, thr, L);
+        if (key < thrL) {
+            const float kth = warp_list_insert<KP>(lk, li, row0 + L, key, id0 + (uint32_t)i, lane);
+            if (lane == L) {
+                thr_own = kth;
+                thr = fminf(thr_own, thr_g);
+            }
+        }
+    }
 }
 
 // Smallest float strictly above v (v finite or +inf).
@@ -197,7 +304,31 @@ struct Work {
     int k_blocks;     // K blocks of BKB bytes
     int64_t n_rows;   // database rows
     int64_t nq_pad;   // n_qtiles * BM
+    // Lockstep over row chunks (see the producer): chunk_tiles tiles per chunk, cpr chunk slots
+    // per round, lag = how many chunks a CTA may run ahead of the slowest CTA of the grid.
+    int chunk_tiles;
+    int cpr;
+    int lag;
+    uint32_t* sync_cnt;  // [rounds * cpr] arrivals per chunk slot, zeroed before the launch
 };
+
+__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Soft wait for a chunk slot to collect `target` arrivals. It only paces the producer for L2
+// locality: on expiry it returns false and the caller stops pacing (no error).
+__device__ __forceinline__ bool wait_arrivals(const uint32_t* p, uint32_t target, uint64_t limit_ns) {
+    if (ld_relaxed(p) >= target) return true;
+    const uint64_t t0 = va::globaltimer_ns();
+    while (ld_relaxed(p) < target) {
+        __nanosleep(128);
+        if (va::globaltimer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
 
 __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int& t0, int& t1) {
     const int s = item / w.n_qtiles;
@@ -256,12 +387,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
+        // Lockstep for L2 reuse: all CTAs of a round stream the same 2-3 row splits; each split
+        // is read by up to one CTA per query tile. Before starting chunk slot g (round * cpr +
+        // local chunk) a CTA waits until every CTA of the grid has started slot g - lag, so the
+        // rows in flight stay within ~lag chunks per split and are fetched from HBM about once.
         if (lane == 0) {
             uint32_t it = 0;
-            for (int item = blockIdx.x; item < n_items && !*s_abort; item += gridDim.x) {
+            int round = 0;
+            bool pace = true;
+            for (int item = blockIdx.x; item < n_items && !*s_abort; item += gridDim.x, ++round) {
                 int qt, t0, t1;
                 item_range(w, item, qt, t0, t1);
+                int next_slot = 0;
                 for (int t = t0; t < t1; ++t) {
+                    const int j = t - t0;
+                    if (j % w.chunk_tiles == 0) {
+                        const int g = round * w.cpr + j / w.chunk_tiles;
+                        if (pace && g >= w.lag) {
+                            const int gr = (g - w.lag) / w.cpr;
+                            const uint32_t target = (uint32_t)min((int)gridDim.x, n_items - gr * (int)gridDim.x);
+                            pace = wait_arrivals(w.sync_cnt + (g - w.lag), target, 200000000ull);
+                        }
+                        atomicAdd(w.sync_cnt + g, 1u);
+                        next_slot = j / w.chunk_tiles + 1;
+                    }
                     for (int kb = 0; kb < w.k_blocks; ++kb, ++it) {
                         const int s = it % stages;
                         const uint32_t ph = (it / stages) & 1u;
@@ -272,6 +421,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_2d(sB + (size_t)s * B_BYTES, &tmap_x, &full[s], kc, t * BN);
                     }
                 }
+                // A shorter item still arrives at every slot of its round.
+                for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
             }
         producer_done:;
         }
@@ -320,17 +471,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int qt, t0, t1;
             item_range(w, item, qt, t0, t1);
             const int64_t q = (int64_t)qt * BM + row;
-            for (int j = 0; j < KP; ++j) {
-                l_key[j * BM + row] = INFINITY;
-                l_id[j * BM + row] = va::kInvalidId;
+            // Reset this warp's 32 row lists (row-contiguous, KP entries each; coalesced).
+            for (int e = lane; e < 32 * KP; e += 32) {
+                l_key[quarter * 32 * KP + e] = INFINITY;
+                l_id[quarter * 32 * KP + e] = va::kInvalidId;
             }
+            __syncwarp();
             float thr_own = INFINITY;
             float thr_g = load_bound(gthr + q);
             float thr = thr_g;
+            // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row): lane j
+            // holds columns j + 32r, r < 8; the next tile's are prefetched while this one runs.
+            float bias[8], nbias[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 7) == 7) {
                     thr_g = load_bound(gthr + q);
                     thr = fminf(thr_own, thr_g);
+                }
+                const int64_t col0 = (int64_t)t * BN;
+                if (t + 1 < t1) {
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) nbias[r] = __ldg(row_bias + col0 + BN + lane + 32 * r);
                 }
                 const uint32_t buf = tile & 1u;
                 const uint32_t tph = (tile >> 1) & 1u;
@@ -341,43 +504,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!ok) goto epi_done;
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-                const int64_t col0 = (int64_t)t * BN;
-                // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row)
-                // live 8 per lane and are broadcast by shuffles.
-                const float4* bp = (const float4*)(row_bias + col0) + lane * 2;
-                const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-                const float bias[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    __syncwarp();
-                    float v[32];
-                    tmem_ld32(taddr + c * 32, v);
-                    const uint32_t cb = (uint32_t)(col0 + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float nb = __shfl_sync(0xFFFFFFFFu, bias[i & 7], c * 4 + (i >> 3));
-                        const float key = fmaf(alpha, v[i], nb);
-                        if (key < thr) {
-                            thr_own = list_insert<KP>(l_key, l_id, row, key, cb + i);
-                            thr = fminf(thr_own, thr_g);
-                        }
-                    }
-                }
+                const uint32_t id0 = (uint32_t)col0;
+                // Four 64-column chunks, TMEM loads double-buffered against the filtering.
+                uint32_t ra[64], rb[64];
+                tmem_ld64(taddr, ra);
+                tmem_wait64(ra);
+                tmem_ld64(taddr + 64, rb);
+                filter_chunk<0, KP>(ra, bias, alpha, id0, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(rb);
+                tmem_ld64(taddr + 128, ra);
+                filter_chunk<1, KP>(rb, bias, alpha, id0 + 64, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(ra);
+                tmem_ld64(taddr + 192, rb);
+                filter_chunk<2, KP>(ra, bias, alpha, id0 + 128, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(rb);
+                // Every TMEM read of this tile is done: hand the accumulator back to the MMA warp.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
+                filter_chunk<3, KP>(rb, bias, alpha, id0 + 192, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
                 // Publish this item's KP-th key (finite once the list is full) as a bound.
                 if (thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
+                // The warp's 32 lists are contiguous in shared memory and in the output
+                // ([split][query][KP]): copy them with coalesced stores.
                 const int s = item / w.n_qtiles;
-                float* pk = part_keys + ((int64_t)s * w.nq_pad + q) * KP;
-                uint32_t* pi = part_ids + ((int64_t)s * w.nq_pad + q) * KP;
-#pragma unroll 4
-                for (int j = 0; j < KP; ++j) {
-                    pk[j] = l_key[j * BM + row];
-                    pi[j] = l_id[j * BM + row];
+                const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
+                for (int e = lane; e < 32 * KP; e += 32) {
+                    part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
+                    part_ids[out0 + e] = l_id[quarter * 32 * KP + e];
                 }
+                __syncwarp();
             }
         }
     epi_done:;
@@ -426,8 +590,20 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
     auto kern = k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nq_pad * sizeof(uint32_t), ctx->stream));
-    kern<<<grid, NUM_THREADS, smem, ctx->stream>>>(mq, mx, w, a.row_bias, a.alpha, a.part_keys, a.part_ids, a.gthr,
-                                                   ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages);
+    VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
+    // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mq, mx, w, a.row_bias, a.alpha, a.part_keys, a.part_ids, a.gthr,
+                                   ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages));
     return va_check_launch("k_tc_filter");
 }
 
@@ -452,6 +628,13 @@ int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan
     plan->splits = splits;
     plan->kp = kp;
     plan->grid = std::min(plan->n_qtiles * splits, g);
+    // Lockstep pacing: chunks of 16 row tiles, a CTA at most 2 chunks ahead of the slowest.
+    plan->chunk_tiles = 16;
+    plan->lag = 2;
+    const int max_item_tiles = (plan->n_tiles + splits - 1) / splits;
+    plan->cpr = (max_item_tiles + plan->chunk_tiles - 1) / plan->chunk_tiles;
+    const int rounds = (plan->n_qtiles * splits + plan->grid - 1) / plan->grid;
+    plan->sync_words = (int64_t)rounds * plan->cpr;
     return VA_OK;
 }
 
@@ -477,6 +660,11 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.k_blocks = (int)((a.dpad * elem + BKB - 1) / BKB);
     w.n_rows = a.n_rows;
     w.nq_pad = p.nq_pad;
+    w.chunk_tiles = p.chunk_tiles;
+    w.cpr = p.cpr;
+    w.lag = p.lag;
+    w.sync_cnt = a.sync_cnt;
+    if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
     const int stages = va_tc_stages(p.kp);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);
     const size_t smem = va_tc_smem_bytes(p.kp, stages);

@@ -13,6 +13,10 @@ struct TcPlan {
     int kp;       // per-query candidate list length
     int grid;
     int64_t nq_pad;
+    int chunk_tiles;     // lockstep pacing: row tiles per chunk
+    int lag;             // chunks a CTA may run ahead of the slowest
+    int cpr;             // chunk slots per round
+    int64_t sync_words;  // size of the pacing counter array
 };
 
 struct TcFilterArgs {
@@ -27,6 +31,8 @@ struct TcFilterArgs {
     float* part_keys;       // [splits][nq_pad][kp]
     uint32_t* part_ids;     // [splits][nq_pad][kp]
     uint32_t* gthr;         // [nq_pad] shared per-query bound (orderable key), set to 0xFF bytes
+    uint32_t* sync_cnt;     // [sync_words] pacing counters, zeroed by va_tc_filter
+    int64_t sync_words;
     unsigned limit_ms;    // bound of every device-side wait
 };
 
