@@ -331,3 +331,29 @@ def test_hamming_knn(ctx, oracle, words, k):
     oi, od = oracle.hamming_knn(q, x, k)
     assert np.array_equal(gd, od)
     assert np.array_equal(gi, oi)  # integer distances: (distance, id) order is exact
+
+
+def test_pair_kernel_parity(oracle, c1, tmp_path):
+    """The cta_group::2 pair kernel (selected per process by VA_TC_PAIR=1) on the C1 workload."""
+    import subprocess
+    import sys
+    x, q, tids, tvals = c1
+    np.save(tmp_path / "x.npy", x)
+    np.save(tmp_path / "q.npy", q)
+    code = (
+        "import sys, numpy as np; sys.path.insert(0, %r)\n"
+        "import vectoraccelerate_b200 as va\n"
+        "x = np.load(%r); q = np.load(%r)\n"
+        "ctx = va.GPUContext(); db = va.Database(ctx, x)\n"
+        "for m in (0, 2):\n"
+        "    v, i = va.knn_search_host(ctx, db, q, 10, m, va.PREC_BF16)\n"
+        "    np.save(%r %% m, v); np.save(%r %% m, i)\n"
+    ) % (ROOT, str(tmp_path / "x.npy"), str(tmp_path / "q.npy"), str(tmp_path / "v%d.npy"),
+         str(tmp_path / "i%d.npy"))
+    env = dict(os.environ, VA_TC_PAIR="1")
+    subprocess.run([sys.executable, "-c", code], check=True, env=env, timeout=600)
+    for metric in (0, 2):
+        vals = np.load(tmp_path / f"v{metric}.npy")
+        ids = np.load(tmp_path / f"i{metric}.npy")
+        frac = _check(oracle, q, x, 10, metric, vals, ids)
+        assert frac >= 0.999

@@ -10,15 +10,22 @@
 //   warp 1        TMEM owner (allocates 2 x 256 fp32 columns) and single-thread MMA issuer:
 //                 4 tcgen05.mma per K block into the current accumulator, tcgen05.commit frees
 //                 the slot; a final commit hands the accumulator to the epilogue
-//   warps 2..5    epilogue: tcgen05.ld 32 columns at a time (one query row per thread), forms
-//                 key = alpha * (q.x) + |x|^2 term, and keeps a per-query sorted list of the KP
-//                 best (key, id) in shared memory, touched only when a key beats the KP-th best
+//   warps 2..5    epilogue: tcgen05.ld 64 columns at a time (one query row per thread, loads
+//                 double-buffered), forms key = alpha * (q.x) + row bias (|x|^2 for L2) with the
+//                 biases broadcast by shuffles, and keeps a sorted list of each query's KP best
+//                 (key, id) in shared memory. A warp-uniform test per 64-column chunk skips the
+//                 lists; otherwise the warp inserts the passing candidates one at a time, all 32
+//                 lanes updating one list (position by ballot, shift by shuffle)
 //
 // Every (query tile, row split) item starts its lists empty, so without help each item would
 // re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share one bound per
 // query in global memory: a finished item publishes its KP-th key (atomicMin on the orderable
 // key); others drop keys above the smallest published bound. The bound is the KP-th key of a
 // subset of rows, never below the global KP-th key, so no candidate of the final pool is lost.
+//
+// The producers of all CTAs advance through row chunks in loose lockstep (each CTA at most two
+// 16-tile chunks ahead of the slowest), so the 2-3 row splits in flight stay in L2 and each row is
+// read from HBM about once per launch (measured 24 GB of DRAM reads for the 15.4 GB operand).
 //
 // Two accumulators let the epilogue of tile t overlap the MMAs of tile t+1. The distance
 // matrix never reaches HBM: per (query tile, row split) work item each query's KP best
@@ -29,6 +36,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "va_internal.cuh"
 #include "va_tc.cuh"
@@ -557,6 +565,310 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
+// ================================================================================================
+// Pair kernel. Two CTAs of a cluster issue cta_group::2 MMAs of M = 256 queries (128 per CTA) by
+// N = 256 rows (128 loaded per CTA), so each SM moves 32 KB of operands per K block instead of
+// 48 KB. The 1-CTA tile's 48 KB of TMA writes plus its tensor-core operand reads per K block
+// oversubscribe the SM's shared-memory and L2 feed (measured: ~54% of the MMA rate with the
+// epilogue removed); the pair halves the B traffic per SM.
+//
+// Protocol (rank 0 = leader, rank 1 = peer; same shared-memory offsets in both CTAs):
+//   producer (both CTAs)  waits its own empty[s]; loads its 128 query rows and 128 tile rows with
+//                         cta_group::2 TMA whose completion counts on the LEADER's full[s]; the
+//                         leader also posts expect_tx for both CTAs' bytes
+//   MMA (leader only)     waits full[s], issues the pair MMAs, commits empty[s] in both CTAs; after
+//                         a tile's last K block commits tfull[buf] in both CTAs; waits the
+//                         leader's tempty[buf], which both CTAs' epilogue warps (8) arrive on
+//   epilogue (both CTAs)  as in the 1-CTA kernel, on its own 128 queries and TMEM
+// No commit or load uses a multicast form: the leader commits twice (own and peer address).
+// ================================================================================================
+constexpr int P_ROWS = 128;                  // rows per CTA of each operand tile
+constexpr int PA_BYTES = P_ROWS * BKB;       // 16 KB of queries
+constexpr int PB_BYTES = P_ROWS * BKB;       // 16 KB of database rows
+constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr int PBM = 256;                     // queries per pair tile
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_index() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+                 : "memory");
+}
+
+template <int ELEM>
+struct PairKind;
+template <>
+struct PairKind<2> {  // bf16 x bf16 -> fp32, M = 256 across the pair
+    static constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(PBM >> 4) << 24);
+    __device__ static __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(acc));
+    }
+};
+template <>
+struct PairKind<4> {  // tf32 x tf32 -> fp32, M = 256 across the pair
+    static constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(PBM >> 4) << 24);
+    __device__ static __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(acc));
+    }
+};
+
+template <int ELEM, int KP>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_tc_filter_pair(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, Work w,
+                     const float* __restrict__ row_bias, float alpha, float* __restrict__ part_keys,
+                     uint32_t* __restrict__ part_ids, uint32_t* __restrict__ gthr, int* err, uint64_t limit_ns,
+                     int stages) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + (size_t)stages * PA_BYTES;
+    float* l_key = (float*)(sB + (size_t)stages * PB_BYTES);  // [128][KP]
+    uint32_t* l_id = (uint32_t*)(l_key + KP * P_ROWS);          // [128][KP]
+    uint64_t* bars = (uint64_t*)(l_id + KP * P_ROWS);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + stages;
+    uint64_t* tfull = bars + 2 * stages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* s_tmem = (uint32_t*)(tempty + 2);
+    volatile int* s_abort = (volatile int*)(s_tmem + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int cid = (int)cluster_index(), ncl = (int)cluster_count();
+    const int n_items = w.n_qtiles * w.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);
+        }
+        *s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
+    }
+    // Both CTAs' barriers exist before either CTA signals the other's.
+    cluster_sync();
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *s_tmem;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer (both CTAs)
+        if (lane == 0) {
+            uint32_t it = 0;
+            int round = 0;
+            bool pace = true;
+            for (int item = cid; item < n_items && !*s_abort; item += ncl, ++round) {
+                int qt, t0, t1;
+                item_range(w, item, qt, t0, t1);
+                int next_slot = 0;
+                for (int t = t0; t < t1; ++t) {
+                    const int j = t - t0;
+                    if (j % w.chunk_tiles == 0) {
+                        const int g = round * w.cpr + j / w.chunk_tiles;
+                        if (pace && g >= w.lag) {
+                            const int gr = (g - w.lag) / w.cpr;
+                            const uint32_t target = 2u * (uint32_t)min(ncl, n_items - gr * ncl);
+                            pace = wait_arrivals(w.sync_cnt + (g - w.lag), target, 200000000ull);
+                        }
+                        atomicAdd(w.sync_cnt + g, 1u);
+                        next_slot = j / w.chunk_tiles + 1;
+                    }
+                    for (int kb = 0; kb < w.k_blocks; ++kb, ++it) {
+                        const int s = it % stages;
+                        const uint32_t ph = (it / stages) & 1u;
+                        if (!mbar_wait(&empty[s], ph ^ 1u, s_abort, err, limit_ns)) goto producer_done;
+                        const uint32_t full_leader = map_rank(smem_u32(&full[s]), 0);
+                        if (leader) mbar_expect_tx(&full[s], 2 * PSTAGE_BYTES);
+                        const int kc = kb * (BKB / ELEM);
+                        tma_load_2d_pair(sA + (size_t)s * PA_BYTES, &tmap_q, full_leader, kc,
+                                         qt * PBM + (int)rank * P_ROWS);
+                        tma_load_2d_pair(sB + (size_t)s * PB_BYTES, &tmap_x, full_leader, kc,
+                                         t * BN + (int)rank * P_ROWS);
+                    }
+                }
+                for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer (leader only)
+        if (leader && lane == 0) {
+            uint32_t it = 0, tile = 0;
+            for (int item = cid; item < n_items && !*s_abort; item += ncl) {
+                int qt, t0, t1;
+                item_range(w, item, qt, t0, t1);
+                for (int t = t0; t < t1; ++t, ++tile) {
+                    const uint32_t buf = tile & 1u;
+                    const uint32_t tph = (tile >> 1) & 1u;
+                    if (!mbar_wait(&tempty[buf], tph ^ 1u, s_abort, err, limit_ns)) goto mma_done;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + buf * BN;
+                    for (int kb = 0; kb < w.k_blocks; ++kb, ++it) {
+                        const int s = it % stages;
+                        const uint32_t ph = (it / stages) & 1u;
+                        if (!mbar_wait(&full[s], ph, s_abort, err, limit_ns)) goto mma_done;
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sA + (size_t)s * PA_BYTES);
+                        const uint32_t b0 = smem_u32(sB + (size_t)s * PB_BYTES);
+#pragma unroll
+                        for (int j = 0; j < BKB / 32; ++j)
+                            PairKind<ELEM>::mma(d_tmem, smem_desc(a0 + 32 * j), smem_desc(b0 + 32 * j),
+                                                (kb | j) ? 1u : 0u);
+                        const uint32_t e = smem_u32(&empty[s]);
+                        mma_commit_pair(map_rank(e, 0));
+                        mma_commit_pair(map_rank(e, 1));
+                    }
+                    const uint32_t f = smem_u32(&tfull[buf]);
+                    mma_commit_pair(map_rank(f, 0));
+                    mma_commit_pair(map_rank(f, 1));
+                }
+            }
+        mma_done:;
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        uint32_t tile = 0;
+        for (int item = cid; item < n_items; item += ncl) {
+            int qt, t0, t1;
+            item_range(w, item, qt, t0, t1);
+            const int64_t qbase = (int64_t)qt * PBM + (int64_t)rank * P_ROWS;
+            const int64_t q = qbase + row;
+            for (int e = lane; e < 32 * KP; e += 32) {
+                l_key[quarter * 32 * KP + e] = INFINITY;
+                l_id[quarter * 32 * KP + e] = va::kInvalidId;
+            }
+            __syncwarp();
+            float thr_own = INFINITY;
+            float thr_g = load_bound(gthr + q);
+            float thr = thr_g;
+            float bias[8], nbias[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
+            for (int t = t0; t < t1; ++t, ++tile) {
+                if (((t - t0) & 7) == 7) {
+                    thr_g = load_bound(gthr + q);
+                    thr = fminf(thr_own, thr_g);
+                }
+                const int64_t col0 = (int64_t)t * BN;
+                if (t + 1 < t1) {
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) nbias[r] = __ldg(row_bias + col0 + BN + lane + 32 * r);
+                }
+                const uint32_t buf = tile & 1u;
+                const uint32_t tph = (tile >> 1) & 1u;
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(&tfull[buf], tph, s_abort, err, limit_ns) ? 1 : 0;
+                ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+                if (!ok) goto epi_done;
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+                const uint32_t id0 = (uint32_t)col0;
+                uint32_t ra[64], rb[64];
+                tmem_ld64(taddr, ra);
+                tmem_wait64(ra);
+                tmem_ld64(taddr + 64, rb);
+                filter_chunk<0, KP>(ra, bias, alpha, id0, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(rb);
+                tmem_ld64(taddr + 128, ra);
+                filter_chunk<1, KP>(rb, bias, alpha, id0 + 64, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(ra);
+                tmem_ld64(taddr + 192, rb);
+                filter_chunk<2, KP>(ra, bias, alpha, id0 + 128, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+                tmem_wait64(rb);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(map_rank(smem_u32(&tempty[buf]), 0));
+                filter_chunk<3, KP>(rb, bias, alpha, id0 + 192, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
+            }
+            {
+                if (thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
+                const int s = item / w.n_qtiles;
+                const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
+                for (int e = lane; e < 32 * KP; e += 32) {
+                    part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
+                    part_ids[out0 + e] = l_id[quarter * 32 * KP + e];
+                }
+                __syncwarp();
+            }
+        }
+    epi_done:;
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    // The peer's last remote arrivals and the pair MMAs are done before either CTA frees TMEM
+    // or exits.
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -586,37 +898,62 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_ele
 
 template <int ELEM, int KP>
 int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t smem, const CUtensorMap& mq,
-                  const CUtensorMap& mx, const Work& w, int grid) {
-    auto kern = k_tc_filter<ELEM, KP>;
+                  const CUtensorMap& mx, const Work& w, int grid, bool pair) {
+    auto kern = pair ? k_tc_filter_pair<ELEM, KP> : k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nq_pad * sizeof(uint32_t), ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
     // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
+    // The pair kernel also runs as clusters of two CTAs.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pair ? 2 : 1;
     VA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mq, mx, w, a.row_bias, a.alpha, a.part_keys, a.part_ids, a.gthr,
                                    ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages));
-    return va_check_launch("k_tc_filter");
+    return va_check_launch(pair ? "k_tc_filter_pair" : "k_tc_filter");
+}
+
+size_t smem_bytes(int kp, int stages, bool pair) {
+    return 1024 + (size_t)stages * (pair ? PSTAGE_BYTES : STAGE_BYTES) + (size_t)kp * BM * 8 + (2 * stages + 4) * 8 +
+           16;
 }
 
 }  // namespace
 
+// The single-CTA kernel is the default; VA_TC_PAIR=1 selects the cta_group::2 pair kernel. At
+// the 10M x 768 headline both run at the same rate, held by the 1 kW power cap (measured: 151.6
+// vs 151.7 ms per launch, sw_power_cap active throughout).
+bool va_tc_use_pair() {
+    static const int v = [] {
+        const char* e = getenv("VA_TC_PAIR");
+        return (e && e[0] == '1') ? 1 : 0;
+    }();
+    return v != 0;
+}
+
 // Plan of a filter launch (host side, shared with va_search.cu).
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan) {
-    plan->n_qtiles = (int)((nq + BM - 1) / BM);
+    const bool pair = va_tc_use_pair() && ctx->sm_count >= 2;
+    const int qrows = pair ? PBM : BM;
+    plan->pair = pair;
+    plan->n_qtiles = (int)((nq + qrows - 1) / qrows);
     plan->n_tiles = (int)((n_rows + BN - 1) / BN);
-    plan->nq_pad = (int64_t)plan->n_qtiles * BM;
-    // Splits: make (query tiles x splits) a multiple of the SM count so every CTA gets the same
-    // number of equally sized items, but never split finer than one row tile.
-    int g = ctx->sm_count;
+    plan->nq_pad = (int64_t)plan->n_qtiles * qrows;
+    // Splits: make (query tiles x splits) a multiple of the number of workers (CTAs, or CTA pairs)
+    // so every worker gets the same number of equally sized items, but never split finer than
+    // one row tile.
+    const int g = pair ? ctx->sm_count / 2 : ctx->sm_count;
     int a = plan->n_qtiles, b = g;
     while (b) {
         int t = a % b;
@@ -627,32 +964,29 @@ int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan
     splits = std::max(1, std::min(splits, plan->n_tiles));
     plan->splits = splits;
     plan->kp = kp;
-    plan->grid = std::min(plan->n_qtiles * splits, g);
+    const int workers = std::min(plan->n_qtiles * splits, g);
+    plan->grid = pair ? 2 * workers : workers;
     // Lockstep pacing: chunks of 16 row tiles, a CTA at most 2 chunks ahead of the slowest.
     plan->chunk_tiles = 16;
     plan->lag = 2;
     const int max_item_tiles = (plan->n_tiles + splits - 1) / splits;
     plan->cpr = (max_item_tiles + plan->chunk_tiles - 1) / plan->chunk_tiles;
-    const int rounds = (plan->n_qtiles * splits + plan->grid - 1) / plan->grid;
+    const int rounds = (plan->n_qtiles * splits + workers - 1) / workers;
     plan->sync_words = (int64_t)rounds * plan->cpr;
     return VA_OK;
 }
 
-size_t va_tc_smem_bytes(int kp, int stages) {
-    return 1024 + (size_t)stages * STAGE_BYTES + (size_t)kp * BM * 8 + (2 * stages + 4) * 8 + 16;
-}
-
-int va_tc_stages(int kp) {
-    for (int s = 6; s >= 2; --s)
-        if (va_tc_smem_bytes(kp, s) <= 227 * 1024) return s;
+int va_tc_stages(int kp, bool pair) {
+    for (int s = pair ? 8 : 6; s >= 2; --s)
+        if (smem_bytes(kp, s, pair) <= 227 * 1024) return s;
     return 0;
 }
 
 int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     const int elem = a.elem_bytes;
     CUtensorMap mq, mx;
-    VA_TRY(make_tmap(&mq, a.q_op, p.nq_pad, a.dpad, elem, BM));
-    VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, elem, BN));
+    VA_TRY(make_tmap(&mq, a.q_op, p.nq_pad, a.dpad, elem, p.pair ? P_ROWS : BM));
+    VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, elem, p.pair ? P_ROWS : BN));
     Work w;
     w.n_qtiles = p.n_qtiles;
     w.splits = p.splits;
@@ -665,15 +999,15 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
     if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
-    const int stages = va_tc_stages(p.kp);
+    const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);
-    const size_t smem = va_tc_smem_bytes(p.kp, stages);
+    const size_t smem = smem_bytes(p.kp, stages, p.pair);
     if (elem == 2) {
-        if (p.kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, p.grid);
-        if (p.kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, p.grid);
+        if (p.kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
     } else {
-        if (p.kp == 32) return launch_filter<4, 32>(ctx, a, stages, smem, mq, mx, w, p.grid);
-        if (p.kp == 64) return launch_filter<4, 64>(ctx, a, stages, smem, mq, mx, w, p.grid);
+        if (p.kp == 32) return launch_filter<4, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 64) return launch_filter<4, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
     }
     return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d not supported by the tensor-core filter", p.kp);
 }

@@ -12,6 +12,7 @@ struct TcPlan {
     int splits;
     int kp;       // per-query candidate list length
     int grid;
+    bool pair;    // cta_group::2 pair kernel (query tiles of 256), else single-CTA (128)
     int64_t nq_pad;
     int chunk_tiles;     // lockstep pacing: row tiles per chunk
     int lag;             // chunks a CTA may run ahead of the slowest
@@ -38,4 +39,5 @@ struct TcFilterArgs {
 
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
 int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
-int va_tc_stages(int kp);
+int va_tc_stages(int kp, bool pair);
+bool va_tc_use_pair();
