@@ -108,20 +108,24 @@ __global__ void k_operand(const void* src, int dtype, int64_t n_valid, int64_t n
 // Per query: select the KP best approximate candidates over all splits, rerank exactly from the
 // original rows, emit the top k sorted by (distance, id).
 constexpr int MR_THREADS = 256;
+constexpr int MR_POOL = 1024;  // candidates kept in shared memory after the bound test
 
 __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
                                                            const uint32_t* __restrict__ part_ids, int splits,
                                                            int64_t nq_pad, int kp, const float* __restrict__ queries,
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
-                                                           int k, uint32_t id_base, float* __restrict__ out_vals,
+                                                           int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
+                                                           float* __restrict__ out_vals,
                                                            uint32_t* __restrict__ out_ids) {
     extern __shared__ uint8_t smem[];
     const int kp2 = va::next_pow2(kp);
     uint64_t* sel = (uint64_t*)smem;       // [kp2]
     uint64_t* ex = sel + kp2;               // [kp2]
-    float* sq = (float*)(ex + kp2);         // [dim]
+    uint64_t* pool = ex + kp2;              // [MR_POOL] candidates at or below the shared bound
+    float* sq = (float*)(pool + MR_POOL);   // [dim]
     __shared__ va::SelectShared sh;
     __shared__ double s_qn;
+    __shared__ int s_cnt;
     const int64_t qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
 
@@ -133,7 +137,28 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         if (id == va::kInvalidId) return ~0ull;
         return va::composite(va::f2key(part_keys[off]), id);
     };
-    const int m = va::block_select_radix((int64_t)splits * kp, kp, get, sel, sh);
+    // The filter's shared bound (smallest KP-th key any work item published for this query) is
+    // at least the global KP-th key, so candidates above it cannot be in the pool: one pass keeps
+    // the rest in shared memory and the selection runs there. If more than MR_POOL survive, the
+    // selection runs over all candidates instead.
+    const int64_t n_all = (int64_t)splits * kp;
+    const uint32_t bound = gthr ? gthr[qi] : 0xFFFFFFFFu;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n_all; i += blockDim.x) {
+        const uint64_t c = get(i);
+        if (c != ~0ull && (uint32_t)(c >> 32) <= bound) {
+            const int slot = atomicAdd(&s_cnt, 1);
+            if (slot < MR_POOL) pool[slot] = c;
+        }
+    }
+    __syncthreads();
+    const int n_pool = s_cnt;
+    int m;
+    if (n_pool <= MR_POOL)
+        m = va::block_select_radix((int64_t)n_pool, kp, [&](int64_t i) -> uint64_t { return pool[i]; }, sel, sh);
+    else
+        m = va::block_select_radix(n_all, kp, get, sel, sh);
     if (metric == VA_METRIC_COSINE && warp == 0) {
         double s = 0;
         for (int j = lane; j < dim; j += 32) s += (double)sq[j] * sq[j];
@@ -237,17 +262,21 @@ int ensure_operand(va_context* ctx, va_database* db, int elem, bool cosine, cons
     return VA_OK;
 }
 
+// Candidate pool per query of the reduced-precision pass: rerank * k when the caller sets the
+// factor, else k plus a margin of max(k / 4, 22) (32 for k = 10, 128 for k = 100); rounded up to
+// a list size the filter supports (32, 64, 128), or 0 when none is large enough.
 int choose_kp(int k, int rerank) {
-    int want = rerank > 0 ? rerank * k : 3 * k;
+    int want = rerank > 0 ? rerank * k : k + std::max(k / 4, 22);
     if (want < k) want = k;
     if (want <= 32) return 32;
     if (want <= 64) return 64;
+    if (want <= 128) return 128;
     return 0;
 }
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
-                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, float* out_vals,
-                 uint32_t* out_ids);
+                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
+                 float* out_vals, uint32_t* out_ids);
 
 int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
               int kp, float* out_vals, uint32_t* out_ids) {
@@ -301,19 +330,19 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
         ctx->prof_n++;
     else
         ctx->k_recorded = true;
-    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, out_vals, out_ids);
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
 }
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
-                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, float* out_vals,
-                 uint32_t* out_ids) {
+                 const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
+                 float* out_vals, uint32_t* out_ids) {
     const int kp2 = va::next_pow2(plan.kp);
-    size_t smem = (size_t)kp2 * 16 + (size_t)db->dim * 4;
+    size_t smem = (size_t)kp2 * 16 + (size_t)MR_POOL * 8 + (size_t)db->dim * 4;
     if (smem > 48 * 1024)
         VA_CUDA_TRY(cudaFuncSetAttribute(k_merge_rerank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
                                                                     plan.kp, queries, db->rows, db->dtype, db->dim,
-                                                                    metric, k, db->id_base, out_vals, out_ids);
+                                                                    metric, k, db->id_base, gthr, out_vals, out_ids);
     return va_check_launch("k_merge_rerank");
 }
 
@@ -457,7 +486,9 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     ctx->k_recorded = false;
     int kp = choose_kp(k, rerank);
     int prec = precision;
-    if (prec == VA_PREC_AUTO) prec = kp ? VA_PREC_BF16 : VA_PREC_FP32;
+    // AUTO: bf16 when the pool holds at least 3k candidates; with a thinner margin (large k) the
+    // 4x smaller tf32 error keeps the true top k inside the pool; no pool size -> exact FP32 route.
+    if (prec == VA_PREC_AUTO) prec = !kp ? VA_PREC_FP32 : (kp >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
     if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
         if (!kp) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
         prec = VA_PREC_BF16;
@@ -467,7 +498,7 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     } else {
         if (!kp)
             return va_set_error(VA_ERR_UNSUPPORTED,
-                                "candidate pool %d x k %d exceeds the tensor-core filter's 64; use precision FP32",
+                                "candidate pool %d x k %d exceeds the tensor-core filter's 128; use precision FP32",
                                 rerank ? rerank : 3, k);
         const int elem = prec == VA_PREC_TF32 ? 4 : 2;
         VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, kp, out_vals, out_ids));
@@ -588,7 +619,7 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
     a.sync_words = plan.sync_words;
     a.limit_ms = 2000u;
     VA_TRY(va_tc_filter(ctx, a, plan));
-    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, out_vals, out_ids);
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
 }
 
 }  // namespace
@@ -609,7 +640,7 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
     VA_REQUIRE(db->ctx->device == ctx->device, "database lives on device %d, context on device %d", db->ctx->device,
                ctx->device);
     const int kp = choose_kp(k, rerank);
-    VA_REQUIRE(kp > 0, "candidate pool of k %d exceeds the tensor-core filter's 64", k);
+    VA_REQUIRE(kp > 0, "candidate pool of k %d exceeds the tensor-core filter's 128", k);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     void* scratch = nullptr;
     VA_TRY(noalloc_scratch(ctx->device, &scratch));

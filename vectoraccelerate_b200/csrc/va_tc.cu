@@ -944,7 +944,9 @@ bool va_tc_use_pair() {
 
 // Plan of a filter launch (host side, shared with va_search.cu).
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan) {
-    const bool pair = va_tc_use_pair() && ctx->sm_count >= 2;
+    // A 128-entry list takes 128 KB of shared memory; the pair kernel's 32 KB stages still leave
+    // room for three of them (the single-CTA kernel would have two).
+    const bool pair = (va_tc_use_pair() || kp >= 128) && ctx->sm_count >= 2;
     const int qrows = pair ? PBM : BM;
     plan->pair = pair;
     plan->n_qtiles = (int)((nq + qrows - 1) / qrows);
@@ -1005,9 +1007,11 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     if (elem == 2) {
         if (p.kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
         if (p.kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 128) return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
     } else {
         if (p.kp == 32) return launch_filter<4, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
         if (p.kp == 64) return launch_filter<4, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 128) return launch_filter<4, 128>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
     }
     return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d not supported by the tensor-core filter", p.kp);
 }
