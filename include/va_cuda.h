@@ -230,6 +230,32 @@ int va_sq_dequantize_int4(va_context* ctx, const uint8_t* in, int64_t n, float s
                           float* out);
 /* Global min and max of x (device reduction); out_minmax[2] is a device pointer. */
 int va_minmax(va_context* ctx, const float* x, int64_t n, float* out_minmax);
+/* Per-dimension min and max of x[n x dim] (device): the statistics the reference's asymmetric
+ * parameters take over the whole array (ScalarQuantizationKernel.swift:509-520), per column. */
+int va_sq_perdim_minmax(va_context* ctx, const float* x, int64_t n, int dim, float* out_min, float* out_max);
+
+/* ------------------------------------------------------------------------------------------ */
+/* int8 scalar-quantized search                                                                */
+/* ------------------------------------------------------------------------------------------ */
+/* Resident int8 database: per-dimension codes of the fp32 rows[n x dim] (host or device), with
+ * scale_j = max((max_j - min_j) / 255, 1e-8) and code = clamp(rint((x - min_j) / scale_j), 0, 255)
+ * - 128 (the asymmetric uint8 mapping of ScalarQuantizationKernel.swift:509-520 applied per
+ * dimension and shifted into int8). mins / maxs (device, [dim]) give the range, e.g. the global
+ * range of a row-sharded database; NULL computes it over these rows. The fp32 rows stay resident
+ * for the exact rerank. */
+int va_db_create_int8(va_context* ctx, const float* rows, int on_device, int64_t n, int dim, const float* mins,
+                      const float* maxs, uint32_t id_base, va_database** out);
+/* Device pointers of an int8 database's parameters and codes (codes row stride in bytes). */
+int va_db_int8_params(const va_database* db, const float** mins, const float** scales, const int8_t** codes,
+                      int* code_stride);
+/* int8 L2 k-NN: queries[nq x dim] fp32 (device) are quantized with the database's parameters;
+ * squared L2 between codes in exact int32 arithmetic (tensor cores) selects the `candidates`
+ * best rows per query by (integer distance, id); those are reranked by exact squared L2 against
+ * the fp32 rows (fp64 accumulation); out_vals/out_ids [nq x k] sorted by (distance, id). No
+ * reference counterpart (the reference has quantizers only, DataTransformations.metal:142-221);
+ * this is the search its int8 storage would feed (IVFQuantizedStorage.swift). */
+int va_int8_knn_search(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int candidates,
+                       float* out_vals, uint32_t* out_ids);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Binary quantization and Hamming (BinaryQuantizationKernel, HammingDistanceKernel)           */
@@ -247,6 +273,16 @@ int va_hamming_matrix(va_context* ctx, const uint32_t* q, int64_t nq, const uint
  * HammingDistanceKernel.swift:114-120,313-363). */
 int va_hamming_knn(va_context* ctx, const uint32_t* q, int64_t nq, const uint32_t* x, int64_t nx, int words, int k,
                    uint32_t* out_dists, uint32_t* out_ids);
+/* Resident binary database of n codes of dim_bits bits (LSB-first uint32 words, as
+ * Metal4BinaryVector, BinaryQuantizationKernel.swift:23-74), host or device. */
+int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
+                        uint32_t id_base, va_database** out);
+/* Batched Hamming k-NN over a binary database on the integer tensor cores: popcount(q ^ x) =
+ * |q| + |x| - 2 q.x over the 0/1 bits, exact; results sorted by (distance, id), k <= 128. Same
+ * results as va_hamming_knn (HammingDistanceKernel.computeBitPacked + nearestNeighbors,
+ * HammingDistanceKernel.swift:114-120,313-363). out_dists may be NULL. */
+int va_hamming_knn_db(va_context* ctx, const va_database* db, const uint32_t* queries, int64_t nq, int k,
+                      uint32_t* out_dists, uint32_t* out_ids);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Seeded synthetic data on the device (restates Tests/.../Utilities/TestRNG.swift:57-161;     */

@@ -75,9 +75,15 @@ SIGNATURES = {
     "va_sq_quantize_int4": [_P, _P, _I64, _F, ctypes.c_int8, _P],
     "va_sq_dequantize_int4": [_P, _P, _I64, _F, ctypes.c_int8, _P],
     "va_minmax": [_P, _P, _I64, _P],
+    "va_sq_perdim_minmax": [_P, _P, _I64, _I, _P, _P],
+    "va_db_create_int8": [_P, _P, _I, _I64, _I, _P, _P, _U32, _PP],
+    "va_db_int8_params": [_P, _P, _P, _P, _P],
+    "va_int8_knn_search": [_P, _P, _P, _I64, _I, _I, _P, _P],
     "va_binary_quantize": [_P, _P, _I64, _I, _F, _P],
     "va_hamming_matrix": [_P, _P, _I64, _P, _I64, _I, _P, _P, _I],
     "va_hamming_knn": [_P, _P, _I64, _P, _I64, _I, _I, _P, _P],
+    "va_db_create_binary": [_P, _P, _I, _I64, _I, _U32, _PP],
+    "va_hamming_knn_db": [_P, _P, _P, _I64, _I, _P, _P],
     "va_gen_gaussian": [_P, _P, _I64, _I, _U64, _I64],
     "va_gen_mixture": [_P, _P, _I64, _I, _U64, _I64, _I, _F, _I],
     "va_f32_to_bf16": [_P, _P, _I64, _P],

@@ -24,6 +24,9 @@ OBJ = os.path.join(HERE, "_build")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
+    # Integer-key filtering orders exact integer distances stored as (subnormal) float bit
+    # patterns: float compares must not flush subnormals.
+    "-ftz=false",
     "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-fvisibility=hidden",
     "-I", os.path.join(ROOT, "include"),

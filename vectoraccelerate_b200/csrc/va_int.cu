@@ -1,0 +1,380 @@
+// va_int.cu -- integer-code search paths on the int8 tensor cores (tcgen05.mma kind::i8, exact
+// int32 accumulation).
+//
+// int8 scalar-quantized L2 (the benchmark's int8 configuration). The reference quantizes with
+// global scales only (ScalarQuantizationKernel.swift:496-520, DataTransformations.metal:174-201);
+// per-dimension codes are this build's definition, shared with the oracle: scale_j =
+// max((max_j - min_j)/255, 1e-8), code = clamp(rint((x - min_j)/scale_j), 0, 255) - 128.
+// L2 on codes is exact in int32 (|c_q|^2 + |c_x|^2 - 2 c_q.c_x <= 768 * 255^2), the top
+// `candidates` codes by (integer distance, id) are reranked exactly against the fp32 rows.
+//
+// Hamming. popcount(q ^ x) of LSB-first packed codes (Metal4BinaryVector.hammingDistance,
+// BinaryQuantizationKernel.swift:65-74) equals |q| + |x| - 2 q.x over the 0/1 expansion of the
+// bits, so the binary database stores its codes as 0/1 bytes and the same integer contraction
+// computes exact Hamming distances; results are ordered by (distance, id) with no rerank.
+#include <algorithm>
+
+#include "va_internal.cuh"
+#include "va_tc.cuh"
+
+extern "C" int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* ids, int nlists,
+                                       int64_t list_stride, int len, int64_t nq, int k, int mode, float* out_vals,
+                                       uint32_t* out_ids);
+int db_create_impl(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype,
+                   uint32_t id_base, va_database** out, bool eager_operand);
+int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
+                             const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,
+                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n);
+
+namespace {
+
+constexpr int CBLOCK = 128;  // int8 operand K granularity (one 128-byte swizzle row)
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+int warps_grid(int64_t warps) { return (int)((warps * 32 + 255) / 256); }
+
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// Per-column min / max (orderable keys, combined with atomics). Block: 8 rows x 32 columns.
+__global__ void k_col_minmax(const float* __restrict__ x, int64_t n, int dim, unsigned* kmin, unsigned* kmax) {
+    const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+    const int rr = threadIdx.x >> 5;
+    float mn = INFINITY, mx = -INFINITY;
+    if (c < dim)
+        for (int64_t r = (int64_t)blockIdx.y * 8 + rr; r < n; r += (int64_t)gridDim.y * 8) {
+            const float v = x[r * dim + c];
+            mn = fminf(mn, v);
+            mx = fmaxf(mx, v);
+        }
+    __shared__ float smn[8][32], smx[8][32];
+    smn[rr][threadIdx.x & 31] = mn;
+    smx[rr][threadIdx.x & 31] = mx;
+    __syncthreads();
+    if (rr == 0 && c < dim) {
+        for (int j = 1; j < 8; ++j) {
+            mn = fminf(mn, smn[j][threadIdx.x]);
+            mx = fmaxf(mx, smx[j][threadIdx.x]);
+        }
+        atomicMin(kmin + c, va::f2key(mn));
+        atomicMax(kmax + c, va::f2key(mx));
+    }
+}
+
+__global__ void k_init_keys(unsigned* kmin, unsigned* kmax, int dim) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
+        kmin[j] = 0xFFFFFFFFu;
+        kmax[j] = 0u;
+    }
+}
+
+__global__ void k_keys_to_minmax(const unsigned* kmin, const unsigned* kmax, int dim, float* mins, float* maxs) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
+        mins[j] = va::key2f(kmin[j]);
+        maxs[j] = va::key2f(kmax[j]);
+    }
+}
+
+// Per-dimension parameters from min / max arrays (in place allowed: mins may alias mn_in, scales
+// may alias mx_in).
+__global__ void k_minmax_to_params(const float* mn_in, const float* mx_in, int dim, float* mins, float* scales) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
+        mins[j] = mn_in[j];
+        scales[j] = fmaxf(__fdiv_rn(mx_in[j] - mn_in[j], 255.0f), 1e-8f);
+    }
+}
+
+// Codes [n_out x cpad] (rows >= n_valid and columns >= dim are 0) and |code|^2 per row. One warp
+// per row. code = clamp(rint((x - min)/scale), 0, 255) - 128 with IEEE division and round half
+// to even, as the oracle computes it.
+__global__ void k_perdim_codes(const float* __restrict__ x, int64_t n_valid, int64_t n_out, int dim, int cpad,
+                               const float* __restrict__ mins, const float* __restrict__ scales, int8_t* __restrict__ out,
+                               int* __restrict__ norms) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_out) return;
+    int acc = 0;
+    for (int j = lane; j < cpad; j += 32) {
+        int c = 0;
+        if (r < n_valid && j < dim) {
+            float u = rintf(__fdiv_rn(x[r * dim + j] - mins[j], scales[j]));
+            u = fminf(255.f, fmaxf(0.f, u));
+            c = (int)u - 128;
+        }
+        out[r * cpad + j] = (int8_t)c;
+        acc += c * c;
+    }
+    acc = warp_sum_i(acc);
+    if (lane == 0 && norms) norms[r] = acc;
+}
+
+// 0/1 bytes of LSB-first packed codes [n_out x cpad] and popcounts. One warp per row.
+__global__ void k_expand_bits(const uint32_t* __restrict__ codes, int64_t n_valid, int64_t n_out, int words, int cpad,
+                              int8_t* __restrict__ out, int* __restrict__ pops) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_out) return;
+    int acc = 0;
+    for (int j = lane; j < cpad; j += 32) {
+        int b = 0;
+        if (r < n_valid && j < words * 32) b = (int)((codes[r * words + (j >> 5)] >> (j & 31)) & 1u);
+        out[r * cpad + j] = (int8_t)b;
+        acc += b;
+    }
+    acc = warp_sum_i(acc);
+    if (lane == 0) pops[r] = acc;
+}
+
+__global__ void k_bits_to_dists(const float* __restrict__ v, const uint32_t* __restrict__ ids, int64_t n,
+                                uint32_t* __restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = ids[i] == va::kInvalidId ? 0xFFFFFFFFu : __float_as_uint(v[i]);
+}
+
+__global__ void k_add_base_ids(uint32_t* ids, int64_t n, uint32_t base) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        if (ids[i] != va::kInvalidId) ids[i] += base;
+}
+
+int pool_list_size(int want) {
+    if (want <= 32) return 32;
+    if (want <= 64) return 64;
+    if (want <= 128) return 128;
+    return 0;
+}
+
+// Filter over the database's integer codes for queries already encoded in q_codes / q_norms
+// (both [plan.nq_pad]); partial lists land in the returned workspace pointers.
+struct IntScratch {
+    int8_t* q_codes;
+    int* q_norms;
+    float* part_keys;
+    uint32_t* part_ids;
+    uint32_t* gthr;
+    uint32_t* sync;
+};
+
+int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntScratch* s) {
+    const size_t qb = (size_t)plan.nq_pad * db->cpad;
+    const size_t part = (size_t)plan.splits * plan.nq_pad * plan.kp;
+    const size_t bytes = round_up((int64_t)qb, 256) + (size_t)plan.nq_pad * 4 + part * 8 + (size_t)plan.nq_pad * 4 +
+                         (size_t)plan.sync_words * 4 + 512;
+    void* ws;
+    VA_TRY(va_workspace(ctx, bytes, &ws));
+    uint8_t* p = (uint8_t*)ws;
+    s->q_codes = (int8_t*)p;
+    p += round_up((int64_t)qb, 256);
+    s->q_norms = (int*)p;
+    s->part_keys = (float*)(s->q_norms + plan.nq_pad);
+    s->part_ids = (uint32_t*)(s->part_keys + part);
+    s->gthr = s->part_ids + part;
+    s->sync = s->gthr + plan.nq_pad;
+    return VA_OK;
+}
+
+int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s) {
+    TcFilterArgs a = {};
+    a.q_op = s.q_codes;
+    a.x_op = db->codes;
+    a.elem_bytes = 1;
+    a.dpad = db->cpad;
+    a.n_rows = db->n;
+    a.row_bias = (const float*)db->code_norms;
+    a.alpha = -2.f;
+    a.row_qn = s.q_norms;
+    a.part_keys = s.part_keys;
+    a.part_ids = s.part_ids;
+    a.gthr = s.gthr;
+    a.sync_cnt = s.sync;
+    a.sync_words = plan.sync_words;
+    a.limit_ms = 2000u;
+    return va_tc_filter(ctx, a, plan);
+}
+
+int alloc_int_db(va_context* ctx, va_database* db, int64_t n, int cpad) {
+    const int64_t n_pad = round_up(n, 256);
+    cudaError_t e = cudaMalloc((void**)&db->codes, (size_t)n * cpad);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&db->code_norms, (size_t)n_pad * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return va_set_error(VA_ERR_OOM, "code allocation (%zu bytes) failed: %s", (size_t)n * cpad,
+                            cudaGetErrorString(e));
+    }
+    VA_CUDA_TRY(cudaMemsetAsync(db->code_norms, 0, (size_t)n_pad * 4, ctx->stream));
+    return VA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int va_sq_perdim_minmax(va_context* ctx, const float* x, int64_t n, int dim, float* out_min, float* out_max) {
+    VA_REQUIRE(ctx && x && out_min && out_max, "ctx, x, out_min and out_max must not be NULL");
+    VA_REQUIRE(n > 0 && dim > 0, "n and dim must be positive");
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    void* ws;
+    VA_TRY(va_workspace(ctx, (size_t)dim * 8, &ws));
+    unsigned* kmin = (unsigned*)ws;
+    unsigned* kmax = kmin + dim;
+    k_init_keys<<<std::max(1, (dim + 255) / 256), 256, 0, ctx->stream>>>(kmin, kmax, dim);
+    dim3 grid((unsigned)((dim + 31) / 32), (unsigned)std::min<int64_t>((n + 7) / 8, 2048));
+    k_col_minmax<<<grid, 256, 0, ctx->stream>>>(x, n, dim, kmin, kmax);
+    k_keys_to_minmax<<<std::max(1, (dim + 255) / 256), 256, 0, ctx->stream>>>(kmin, kmax, dim, out_min, out_max);
+    return va_check_launch("k_col_minmax");
+}
+
+int va_db_create_int8(va_context* ctx, const float* rows, int on_device, int64_t n, int dim, const float* mins,
+                      const float* maxs, uint32_t id_base, va_database** out) {
+    VA_REQUIRE(ctx && rows && out, "ctx, rows and out must not be NULL");
+    VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
+    VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
+    VA_REQUIRE(dim <= VA_MAX_DIM, "dimension %d exceeds maximum supported dimension %d", dim, VA_MAX_DIM);
+    VA_REQUIRE((mins == nullptr) == (maxs == nullptr), "mins and maxs must be both given or both NULL");
+    VA_REQUIRE((uint64_t)n + id_base <= 0xFFFFFFFFull, "numDataset + id_base exceeds the uint32 id range");
+    *out = nullptr;
+    va_database* db = nullptr;
+    VA_TRY(db_create_impl(ctx, rows, on_device, n, dim, VA_DTYPE_F32, id_base, &db, false));
+    db->kind = VA_DB_INT8;
+    db->cpad = (int)round_up(dim, CBLOCK);
+    int s = alloc_int_db(ctx, db, n, db->cpad);
+    if (s == VA_OK && (cudaMalloc((void**)&db->sq_mins, (size_t)dim * 4) != cudaSuccess ||
+                       cudaMalloc((void**)&db->sq_scales, (size_t)dim * 4) != cudaSuccess)) {
+        cudaGetLastError();
+        s = va_set_error(VA_ERR_OOM, "parameter allocation failed");
+    }
+    if (s == VA_OK) {
+        if (mins) {
+            k_minmax_to_params<<<std::max(1, (dim + 255) / 256), 256, 0, ctx->stream>>>(mins, maxs, dim, db->sq_mins,
+                                                                                       db->sq_scales);
+            s = va_check_launch("k_minmax_to_params");
+        } else {
+            s = va_sq_perdim_minmax(ctx, (const float*)db->rows, n, dim, db->sq_mins, db->sq_scales);
+            if (s == VA_OK) {
+                k_minmax_to_params<<<std::max(1, (dim + 255) / 256), 256, 0, ctx->stream>>>(
+                    db->sq_mins, db->sq_scales, dim, db->sq_mins, db->sq_scales);
+                s = va_check_launch("k_minmax_to_params");
+            }
+        }
+    }
+    if (s == VA_OK) {
+        k_perdim_codes<<<warps_grid(n), 256, 0, ctx->stream>>>((const float*)db->rows, n, n, dim, db->cpad,
+                                                              db->sq_mins, db->sq_scales, db->codes, db->code_norms);
+        s = va_check_launch("k_perdim_codes");
+    }
+    if (s != VA_OK) {
+        va_db_destroy(db);
+        return s;
+    }
+    *out = db;
+    return VA_OK;
+}
+
+int va_db_int8_params(const va_database* db, const float** mins, const float** scales, const int8_t** codes,
+                      int* code_stride) {
+    VA_REQUIRE(db, "db must not be NULL");
+    VA_REQUIRE(db->kind == VA_DB_INT8, "database is not an int8 database");
+    if (mins) *mins = db->sq_mins;
+    if (scales) *scales = db->sq_scales;
+    if (codes) *codes = db->codes;
+    if (code_stride) *code_stride = db->cpad;
+    return VA_OK;
+}
+
+int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int candidates,
+                       float* out_vals, uint32_t* out_ids) {
+    VA_REQUIRE(ctx && cdb && queries && out_vals && out_ids, "all pointers must be non-NULL");
+    VA_REQUIRE(cdb->kind == VA_DB_INT8, "database is not an int8 database (use va_db_create_int8)");
+    VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
+    VA_REQUIRE(k > 0, "k must be positive, got %d", k);
+    VA_REQUIRE(candidates >= k, "candidates %d must be >= k %d", candidates, k);
+    const int kp = pool_list_size(candidates);
+    VA_REQUIRE(kp > 0, "candidates %d exceeds the supported pool of 128", candidates);
+    va_database* db = const_cast<va_database*>(cdb);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    TcPlan plan;
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    IntScratch s;
+    VA_TRY(int_scratch(ctx, db, plan, &s));
+    k_perdim_codes<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, db->dim, db->cpad,
+                                                                     db->sq_mins, db->sq_scales, s.q_codes, s.q_norms);
+    VA_TRY(va_check_launch("k_perdim_codes(queries)"));
+    VA_TRY(run_int_filter(ctx, db, plan, s));
+    return va_merge_rerank_internal(ctx, db, queries, nq, k, VA_METRIC_L2SQ, plan, s.part_keys, s.part_ids, s.gthr,
+                                    out_vals, out_ids, candidates);
+}
+
+int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
+                        uint32_t id_base, va_database** out) {
+    VA_REQUIRE(ctx && codes && out, "ctx, codes and out must not be NULL");
+    VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
+    VA_REQUIRE(dim_bits > 0 && dim_bits <= 8192, "dimension must be in 1..8192 bits, got %d", dim_bits);
+    VA_REQUIRE((uint64_t)n + id_base <= 0xFFFFFFFFull, "numDataset + id_base exceeds the uint32 id range");
+    *out = nullptr;
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    va_database* db = new va_database();
+    db->ctx = ctx;
+    db->n = n;
+    db->dim = dim_bits;
+    db->dtype = VA_DTYPE_F32;
+    db->id_base = id_base;
+    db->kind = VA_DB_BINARY;
+    db->words = (dim_bits + 31) / 32;
+    db->cpad = (int)round_up((int64_t)db->words * 32, CBLOCK);
+    const size_t pbytes = (size_t)n * db->words * 4;
+    cudaError_t e = cudaMalloc(&db->rows, pbytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        delete db;
+        return va_set_error(VA_ERR_OOM, "code allocation (%zu bytes) failed", pbytes);
+    }
+    int s = VA_OK;
+    e = cudaMemcpyAsync(db->rows, codes, pbytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                        ctx->stream);
+    if (e != cudaSuccess) s = va_set_error(VA_ERR_CUDA, "code upload failed: %s", cudaGetErrorString(e));
+    if (s == VA_OK) s = alloc_int_db(ctx, db, n, db->cpad);
+    if (s == VA_OK) {
+        k_expand_bits<<<warps_grid(n), 256, 0, ctx->stream>>>((const uint32_t*)db->rows, n, n, db->words, db->cpad,
+                                                             db->codes, db->code_norms);
+        s = va_check_launch("k_expand_bits");
+    }
+    if (s != VA_OK) {
+        va_db_destroy(db);
+        return s;
+    }
+    *out = db;
+    return VA_OK;
+}
+
+int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* queries, int64_t nq, int k,
+                      uint32_t* out_dists, uint32_t* out_ids) {
+    VA_REQUIRE(ctx && cdb && queries && out_ids, "ctx, db, queries and out_ids must not be NULL");
+    VA_REQUIRE(cdb->kind == VA_DB_BINARY, "database is not a binary database (use va_db_create_binary)");
+    VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
+    VA_REQUIRE(k > 0 && k <= 128, "k must be between 1 and 128 for the binary search, got %d", k);
+    va_database* db = const_cast<va_database*>(cdb);
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    const int kp = pool_list_size(k);
+    TcPlan plan;
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    IntScratch s;
+    VA_TRY(int_scratch(ctx, db, plan, &s));
+    void* ws2;
+    const size_t extra = (size_t)nq * k * 8;
+    VA_TRY(va_io_buffer(ctx, extra + 256, &ws2));
+    float* mv = (float*)ws2;
+    k_expand_bits<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, db->words, db->cpad,
+                                                                    s.q_codes, s.q_norms);
+    VA_TRY(va_check_launch("k_expand_bits(queries)"));
+    VA_TRY(run_int_filter(ctx, db, plan, s));
+    VA_TRY(va_merge_lists_internal(ctx, s.part_keys, s.part_ids, plan.splits, plan.nq_pad * plan.kp, plan.kp, nq, k,
+                                   VA_SELECT_MIN, mv, out_ids));
+    const int blocks = std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096));
+    if (out_dists) k_bits_to_dists<<<blocks, 256, 0, ctx->stream>>>(mv, out_ids, nq * k, out_dists);
+    if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
+    return va_check_launch("k_bits_to_dists");
+}
+
+}  // extern "C"

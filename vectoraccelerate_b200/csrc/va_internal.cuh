@@ -84,7 +84,19 @@ struct va_database {
     int dpad = 0;                // dim rounded up to the tensor-core K block (64)
     bool op_alias = false;       // op aliases rows (bf16 rows with dim % 64 == 0)
     bool op_f32_alias = false;   // op_f32 aliases rows (fp32 rows with dim % 64 == 0)
+    // Integer databases (int8 per-dimension codes, or 0/1 bytes of binary codes).
+    int kind = 0;                // 0 float rows, 1 int8 codes of fp32 rows, 2 binary codes
+    int8_t* codes = nullptr;     // [n x cpad] int8 tensor-core operand, zero padded
+    int* code_norms = nullptr;   // |code|^2 (int8) or popcount (binary); padded to 256 rows
+    float* sq_mins = nullptr;    // int8: per-dimension minimum
+    float* sq_scales = nullptr;  // int8: per-dimension scale
+    int cpad = 0;                // code row length (multiple of 128)
+    int words = 0;               // binary: 32-bit words per code
 };
+
+#define VA_DB_FLOAT 0
+#define VA_DB_INT8 1
+#define VA_DB_BINARY 2
 
 // ------------------------------------------------------------------------------------------------
 // Device helpers

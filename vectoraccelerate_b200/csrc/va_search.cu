@@ -112,7 +112,8 @@ constexpr int MR_POOL = 1024;  // candidates kept in shared memory after the bou
 
 __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
                                                            const uint32_t* __restrict__ part_ids, int splits,
-                                                           int64_t nq_pad, int kp, const float* __restrict__ queries,
+                                                           int64_t nq_pad, int kp, int pool_n,
+                                                           const float* __restrict__ queries,
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
                                                            int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
                                                            float* __restrict__ out_vals,
@@ -155,10 +156,11 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
     __syncthreads();
     const int n_pool = s_cnt;
     int m;
+    // Exactly pool_n (<= kp) best candidates by (key, id) go to the rerank.
     if (n_pool <= MR_POOL)
-        m = va::block_select_radix((int64_t)n_pool, kp, [&](int64_t i) -> uint64_t { return pool[i]; }, sel, sh);
+        m = va::block_select_radix((int64_t)n_pool, pool_n, [&](int64_t i) -> uint64_t { return pool[i]; }, sel, sh);
     else
-        m = va::block_select_radix(n_all, kp, get, sel, sh);
+        m = va::block_select_radix(n_all, pool_n, get, sel, sh);
     if (metric == VA_METRIC_COSINE && warp == 0) {
         double s = 0;
         for (int j = lane; j < dim; j += 32) s += (double)sq[j] * sq[j];
@@ -276,7 +278,7 @@ int choose_kp(int k, int rerank) {
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids);
+                 float* out_vals, uint32_t* out_ids, int pool_n = 0);
 
 int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
               int kp, float* out_vals, uint32_t* out_ids) {
@@ -307,7 +309,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
     VA_TRY(va_check_launch("k_operand(queries)"));
 
-    TcFilterArgs a;
+    TcFilterArgs a = {};
     a.q_op = q_op;
     a.x_op = x_op;
     a.elem_bytes = elem;
@@ -335,13 +337,14 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids) {
+                 float* out_vals, uint32_t* out_ids, int pool_n) {
     const int kp2 = va::next_pow2(plan.kp);
     size_t smem = (size_t)kp2 * 16 + (size_t)MR_POOL * 8 + (size_t)db->dim * 4;
     if (smem > 48 * 1024)
         VA_CUDA_TRY(cudaFuncSetAttribute(k_merge_rerank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
-                                                                    plan.kp, queries, db->rows, db->dtype, db->dim,
+                                                                    plan.kp, pool_n > 0 ? pool_n : plan.kp, queries,
+                                                                    db->rows, db->dtype, db->dim,
                                                                     metric, k, db->id_base, gthr, out_vals, out_ids);
     return va_check_launch("k_merge_rerank");
 }
@@ -386,10 +389,10 @@ int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t 
 
 }  // namespace
 
-extern "C" {
-
-int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype, uint32_t id_base,
-                 va_database** out) {
+// Database of original rows with norms; eager_operand also builds the bf16 tensor-core operand
+// (integer databases skip it: they search their own codes).
+int db_create_impl(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype,
+                   uint32_t id_base, va_database** out, bool eager_operand) {
     VA_REQUIRE(ctx && rows && out, "ctx, rows and out must not be NULL");
     VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
     VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
@@ -426,7 +429,7 @@ int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, in
     }
     k_row_bias<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2, db->zbias);
     int s = va_check_launch("k_row_bias");
-    if (s == VA_OK) {
+    if (s == VA_OK && eager_operand) {
         // The bf16 operand serves the default precision: build it now so searches only read.
         const void* op;
         s = ensure_operand(ctx, db, 2, false, &op);
@@ -439,6 +442,13 @@ int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, in
     return VA_OK;
 }
 
+extern "C" {
+
+int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype, uint32_t id_base,
+                 va_database** out) {
+    return db_create_impl(ctx, rows, on_device, n, dim, dtype, id_base, out, true);
+}
+
 int va_db_destroy(va_database* db) {
     if (!db) return VA_OK;
     cudaSetDevice(db->ctx->device);
@@ -449,6 +459,10 @@ int va_db_destroy(va_database* db) {
     if (db->op_f32_cos) cudaFree(db->op_f32_cos);
     if (db->norms2) cudaFree(db->norms2);
     if (db->zbias) cudaFree(db->zbias);
+    if (db->codes) cudaFree(db->codes);
+    if (db->code_norms) cudaFree(db->code_norms);
+    if (db->sq_mins) cudaFree(db->sq_mins);
+    if (db->sq_scales) cudaFree(db->sq_scales);
     if (db->rows) cudaFree(db->rows);
     delete db;
     return VA_OK;
@@ -471,6 +485,7 @@ int va_db_rows(const va_database* db, const void** rows) {
 int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int metric,
                   int precision, int rerank, float* out_vals, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
+    VA_REQUIRE(cdb->kind != VA_DB_BINARY, "a binary database is searched with va_hamming_knn_db");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(queries, "queries must not be NULL");
     VA_REQUIRE(k > 0, "k must be positive, got %d", k);
@@ -604,7 +619,7 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
         k_operand<float><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
     VA_TRY(va_check_launch("k_operand(queries)"));
-    TcFilterArgs a;
+    TcFilterArgs a = {};
     a.q_op = q_op;
     a.x_op = x_op;
     a.elem_bytes = elem;
@@ -627,6 +642,7 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
 extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k,
                                      int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
+    VA_REQUIRE(cdb->kind != VA_DB_BINARY, "a binary database is searched with va_hamming_knn_db");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(queries, "queries must not be NULL");
     VA_REQUIRE(k > 0, "k must be positive, got %d", k);
@@ -647,4 +663,11 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
     const int elem = precision == VA_PREC_TF32 ? 4 : 2;
     return search_tc_fixed(ctx, db, queries, nq, k, metric, elem, kp, (uint8_t*)scratch, VA_NOALLOC_SCRATCH_BYTES,
                            out_vals, out_ids);
+}
+
+// Internal entry of the merge + exact rerank step for other translation units (the int8 path).
+int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
+                             const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,
+                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n) {
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool_n);
 }

@@ -133,6 +133,18 @@ struct Kind<2> {  // bf16 x bf16 -> fp32
     }
 };
 template <>
+struct Kind<1> {  // s8 x s8 -> s32 (exact)
+    static constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+    __device__ static __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(acc));
+    }
+};
+template <>
 struct Kind<4> {  // tf32 x tf32 -> fp32
     static constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                       ((uint32_t)(BM >> 4) << 24);
@@ -242,17 +254,26 @@ __device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r
 // when some lane's minimum beats its threshold: each lane marks its passing columns; the warp
 // then inserts the marked candidates one at a time (lowest lane first, each lane in column
 // order), re-checking each against the owning lane's current threshold.
-template <int C, int KP>
-__device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bias)[8], float alpha, uint32_t id0,
-                                             float* lk, uint32_t* li, int row0, int lane, float thr_g,
-                                             float& thr_own, float& thr) {
+//
+// Integer mode (INTK, int8 codes with int32 accumulation): the key is the exact integer distance
+// bias - 2 * acc + qn (bias = |x|^2 of the codes, or |x| of 0/1 codes; qn the same for the
+// query), stored as the bit pattern of a non-negative float, which orders like the integer. Rows
+// past n_rows are excluded by id in the cold path.
+template <int C, int KP, bool INTK>
+__device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bias)[8], float alpha, int qn,
+                                             uint32_t id0, uint32_t n_rows, float* lk, uint32_t* li, int row0,
+                                             int lane, float thr_g, float& thr_own, float& thr) {
     float mn[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) mn[j] = INFINITY;
 #pragma unroll
     for (int i = 0; i < 64; ++i) {
         const float b = __shfl_sync(0xFFFFFFFFu, bias[2 * C + (i >> 5)], i & 31);
-        const float key = fmaf(alpha, __uint_as_float(r[i]), b);
+        float key;
+        if constexpr (INTK)
+            key = __int_as_float(__float_as_int(b) - 2 * (int)r[i] + qn);
+        else
+            key = fmaf(alpha, __uint_as_float(r[i]), b);
         r[i] = __float_as_uint(key);
         mn[i & 7] = fminf(mn[i & 7], key);
     }
@@ -282,7 +303,7 @@ __device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bi
         i = __shfl_sync(0xFFFFFFFFu, i, L);
         key = __shfl_sync(0xFFFFFFFFu, key, L);
         const float thrL = __shfl_sync(0xFFFFFFFFu, thr, L);
-        if (key < thrL) {
+        if (key < thrL && id0 + (uint32_t)i < n_rows) {
             const float kth = warp_list_insert<KP>(lk, li, row0 + L, key, id0 + (uint32_t)i, lane);
             if (lane == L) {
                 thr_own = kth;
@@ -348,7 +369,8 @@ __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int
 template <int ELEM, int KP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_tc_filter(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, Work w,
-                const float* __restrict__ row_bias, float alpha, float* __restrict__ part_keys,
+                const float* __restrict__ row_bias, float alpha, const int* __restrict__ row_qn,
+                float* __restrict__ part_keys,
                 uint32_t* __restrict__ part_ids, uint32_t* __restrict__ gthr, int* err, uint64_t limit_ns,
                 int stages) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -485,6 +507,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 l_id[quarter * 32 * KP + e] = va::kInvalidId;
             }
             __syncwarp();
+            const int qn = row_qn ? row_qn[q] : 0;
+            const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
             float thr_g = load_bound(gthr + q);
             float thr = thr_g;
@@ -518,22 +542,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tmem_ld64(taddr, ra);
                 tmem_wait64(ra);
                 tmem_ld64(taddr + 64, rb);
-                filter_chunk<0, KP>(ra, bias, alpha, id0, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<0, KP, (ELEM == 1)>(ra, bias, alpha, qn, id0, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(rb);
                 tmem_ld64(taddr + 128, ra);
-                filter_chunk<1, KP>(rb, bias, alpha, id0 + 64, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<1, KP, (ELEM == 1)>(rb, bias, alpha, qn, id0 + 64, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(ra);
                 tmem_ld64(taddr + 192, rb);
-                filter_chunk<2, KP>(ra, bias, alpha, id0 + 128, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<2, KP, (ELEM == 1)>(ra, bias, alpha, qn, id0 + 128, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(rb);
                 // Every TMEM read of this tile is done: hand the accumulator back to the MMA warp.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
-                filter_chunk<3, KP>(rb, bias, alpha, id0 + 192, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<3, KP, (ELEM == 1)>(rb, bias, alpha, qn, id0 + 192, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
 #pragma unroll
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
@@ -643,6 +667,18 @@ struct PairKind<2> {  // bf16 x bf16 -> fp32, M = 256 across the pair
     }
 };
 template <>
+struct PairKind<1> {  // s8 x s8 -> s32, M = 256 across the pair
+    static constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(PBM >> 4) << 24);
+    __device__ static __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(acc));
+    }
+};
+template <>
 struct PairKind<4> {  // tf32 x tf32 -> fp32, M = 256 across the pair
     static constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                       ((uint32_t)(PBM >> 4) << 24);
@@ -658,7 +694,8 @@ struct PairKind<4> {  // tf32 x tf32 -> fp32, M = 256 across the pair
 template <int ELEM, int KP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_tc_filter_pair(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, Work w,
-                     const float* __restrict__ row_bias, float alpha, float* __restrict__ part_keys,
+                     const float* __restrict__ row_bias, float alpha, const int* __restrict__ row_qn,
+                float* __restrict__ part_keys,
                      uint32_t* __restrict__ part_ids, uint32_t* __restrict__ gthr, int* err, uint64_t limit_ns,
                      int stages) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -796,6 +833,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 l_id[quarter * 32 * KP + e] = va::kInvalidId;
             }
             __syncwarp();
+            const int qn = row_qn ? row_qn[q] : 0;
+            const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
             float thr_g = load_bound(gthr + q);
             float thr = thr_g;
@@ -825,21 +864,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tmem_ld64(taddr, ra);
                 tmem_wait64(ra);
                 tmem_ld64(taddr + 64, rb);
-                filter_chunk<0, KP>(ra, bias, alpha, id0, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<0, KP, (ELEM == 1)>(ra, bias, alpha, qn, id0, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(rb);
                 tmem_ld64(taddr + 128, ra);
-                filter_chunk<1, KP>(rb, bias, alpha, id0 + 64, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<1, KP, (ELEM == 1)>(rb, bias, alpha, qn, id0 + 64, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(ra);
                 tmem_ld64(taddr + 192, rb);
-                filter_chunk<2, KP>(ra, bias, alpha, id0 + 128, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<2, KP, (ELEM == 1)>(ra, bias, alpha, qn, id0 + 128, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
                 tmem_wait64(rb);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_remote(map_rank(smem_u32(&tempty[buf]), 0));
-                filter_chunk<3, KP>(rb, bias, alpha, id0 + 192, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
+                filter_chunk<3, KP, (ELEM == 1)>(rb, bias, alpha, qn, id0 + 192, n_rows32, l_key, l_id, quarter * 32, lane, thr_g, thr_own, thr);
                 __syncwarp();
 #pragma unroll
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
@@ -888,7 +927,10 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_ele
     cuuint64_t strides[1] = {(cuuint64_t)(cols_elems * elem_bytes)};
     cuuint32_t box[2] = {(cuuint32_t)(BKB / elem_bytes), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+    const CUtensorMapDataType dt = elem_bytes == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    CUresult r = enc(map, dt, 2,
                      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -919,8 +961,8 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pair ? 2 : 1;
-    VA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mq, mx, w, a.row_bias, a.alpha, a.part_keys, a.part_ids, a.gthr,
-                                   ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages));
+    VA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mq, mx, w, a.row_bias, a.alpha, a.row_qn, a.part_keys, a.part_ids,
+                                   a.gthr, ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages));
     return va_check_launch(pair ? "k_tc_filter_pair" : "k_tc_filter");
 }
 
@@ -1004,7 +1046,11 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);
     const size_t smem = smem_bytes(p.kp, stages, p.pair);
-    if (elem == 2) {
+    if (elem == 1) {
+        if (p.kp == 32) return launch_filter<1, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 64) return launch_filter<1, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+        if (p.kp == 128) return launch_filter<1, 128>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
+    } else if (elem == 2) {
         if (p.kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
         if (p.kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
         if (p.kp == 128) return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);

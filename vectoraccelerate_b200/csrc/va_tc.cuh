@@ -23,12 +23,14 @@ struct TcPlan {
 struct TcFilterArgs {
     const void* q_op;     // queries, [nq_pad x dpad] bf16 or fp32, zero padded
     const void* x_op;     // rows, [n_rows x dpad] bf16 or fp32, zero padded
-    int elem_bytes;       // 2 = bf16 (kind::f16), 4 = fp32 read as tf32 (kind::tf32)
+    int elem_bytes;       // 1 = int8 (kind::i8, exact), 2 = bf16 (kind::f16), 4 = fp32 as tf32 (kind::tf32)
     int64_t dpad;         // padded row length in elements (multiple of 64)
     int64_t n_rows;
     const float* row_bias;  // per row: |x|^2 (L2) or 0 (IP, cosine); +inf for the rows past n_rows
                             // up to a multiple of 256 (those never pass the filter)
-    float alpha;            // key = alpha * dot + row_bias
+    float alpha;            // key = alpha * dot + row_bias (float operands)
+    const int* row_qn;      // int8 operands: per query |code|^2 (or |code| of 0/1 codes); the key is
+                            // then the exact integer row_bias - 2 * dot + row_qn (row_bias holds ints)
     float* part_keys;       // [splits][nq_pad][kp]
     uint32_t* part_ids;     // [splits][nq_pad][kp]
     uint32_t* gthr;         // [nq_pad] shared per-query bound (orderable key), set to 0xFF bytes

@@ -491,3 +491,116 @@ class HammingDistanceKernel(_Kernel):
         oi = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
         _ffi.call("va_hamming_knn", self._h, dq.ptr, q.shape[0], dx.ptr, x.shape[0], q.shape[1], k, od.ptr, oi.ptr)
         return od.download(), oi.download()
+
+
+class _DbHandle:
+    def close(self):
+        if getattr(self, "handle", None):
+            _ffi.call("va_db_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            if getattr(self, "handle", None):
+                _ffi.load().va_db_destroy(self.handle)
+        except Exception:
+            pass
+
+
+class Int8Database(_DbHandle):
+    """Resident int8 scalar-quantized database: per-dimension codes of fp32 rows plus the rows
+    themselves for the exact rerank. Quantization: scale_j = max((max_j - min_j)/255, 1e-8),
+    code = clamp(rint((x - min_j)/scale_j), 0, 255) - 128 (the asymmetric uint8 mapping of
+    ScalarQuantizationKernel.swift:509-520 per dimension). `mins`/`maxs` fix the range (e.g. the
+    global range of a sharded database); by default it is taken over these rows."""
+
+    def __init__(self, context: GPUContext, rows=None, id_base: int = 0, mins=None, maxs=None,
+                 device_ptr: int | None = None, n: int | None = None, dim: int | None = None):
+        self.context = context
+        h = ctypes.c_void_p()
+        dmn = dmx = None
+        if mins is not None:
+            dmn = context.get_buffer_for(np.ascontiguousarray(mins, np.float32))
+            dmx = context.get_buffer_for(np.ascontiguousarray(maxs, np.float32))
+        pmn = dmn.ptr if dmn else None
+        pmx = dmx.ptr if dmx else None
+        if device_ptr is not None:
+            _ffi.call("va_db_create_int8", context.handle, device_ptr, 1, n, dim, pmn, pmx, id_base, ctypes.byref(h))
+            self.n, self.dim = n, dim
+        else:
+            a = _f32(rows)
+            _ffi.call("va_db_create_int8", context.handle, a.ctypes.data_as(_vp), 0, a.shape[0], a.shape[1], pmn, pmx,
+                      id_base, ctypes.byref(h))
+            self.n, self.dim = a.shape
+        context.synchronize()
+        self.handle = h.value
+        self.id_base = id_base
+
+    def parameters(self):
+        """(mins, scales) as numpy arrays."""
+        pm, ps = ctypes.c_void_p(), ctypes.c_void_p()
+        _ffi.call("va_db_int8_params", self.handle, ctypes.byref(pm), ctypes.byref(ps), None, None)
+        mins = np.empty(self.dim, np.float32)
+        scales = np.empty(self.dim, np.float32)
+        _ffi.call("va_buffer_download", self.context.handle, mins.ctypes.data_as(_vp), pm.value,
+                  ctypes.c_size_t(mins.nbytes))
+        _ffi.call("va_buffer_download", self.context.handle, scales.ctypes.data_as(_vp), ps.value,
+                  ctypes.c_size_t(scales.nbytes))
+        self.context.synchronize()
+        return mins, scales
+
+    def codes(self) -> np.ndarray:
+        """The int8 codes [n x dim]."""
+        pc, stride = ctypes.c_void_p(), ctypes.c_int()
+        _ffi.call("va_db_int8_params", self.handle, None, None, ctypes.byref(pc), ctypes.byref(stride))
+        out = np.empty((self.n, stride.value), np.int8)
+        _ffi.call("va_buffer_download", self.context.handle, out.ctypes.data_as(_vp), pc.value,
+                  ctypes.c_size_t(out.nbytes))
+        self.context.synchronize()
+        return out[:, : self.dim].copy()
+
+    def search(self, queries, k: int, candidates: int):
+        """int8 L2 k-NN with exact rerank of `candidates` per query -> (values, ids) numpy."""
+        q = _f32(queries)
+        if q.shape[1] != self.dim:
+            raise InvalidInput(f"query dimension {q.shape[1]} != database dimension {self.dim}")
+        ctx = self.context
+        dq = ctx.get_buffer_for(q)
+        ov = ctx.get_buffer(4 * q.shape[0] * k, np.float32, (q.shape[0], k))
+        oi = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
+        _ffi.call("va_int8_knn_search", ctx.handle, self.handle, dq.ptr, q.shape[0], k, candidates, ov.ptr, oi.ptr)
+        return ov.download(), oi.download()
+
+
+class BinaryDatabase(_DbHandle):
+    """Resident binary database of LSB-first packed codes (Metal4BinaryVector layout,
+    BinaryQuantizationKernel.swift:23-74) searched by Hamming distance on the integer tensor
+    cores; the same results as HammingDistanceKernel.nearest_neighbors."""
+
+    def __init__(self, context: GPUContext, codes, dim_bits: int | None = None, id_base: int = 0):
+        self.context = context
+        c = np.ascontiguousarray(codes, np.uint32)
+        if c.ndim != 2:
+            raise InvalidInput("codes must be a 2-D array of uint32 words")
+        self.n, self.words = c.shape
+        self.dim_bits = dim_bits or self.words * 32
+        h = ctypes.c_void_p()
+        _ffi.call("va_db_create_binary", context.handle, c.ctypes.data_as(_vp), 0, self.n, self.dim_bits, id_base,
+                  ctypes.byref(h))
+        context.synchronize()
+        self.handle = h.value
+        self.id_base = id_base
+
+    def search(self, query_codes, k: int):
+        """-> (distances uint32 [Q,k], ids uint32 [Q,k]), sorted by (distance, id)."""
+        q = np.ascontiguousarray(query_codes, np.uint32)
+        if q.ndim == 1:
+            q = q[None, :]
+        if q.shape[1] != self.words:
+            raise InvalidInput(f"query words {q.shape[1]} != database words {self.words}")
+        ctx = self.context
+        dq = ctx.get_buffer_for(q)
+        od = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
+        oi = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
+        _ffi.call("va_hamming_knn_db", ctx.handle, self.handle, dq.ptr, q.shape[0], k, od.ptr, oi.ptr)
+        return od.download(), oi.download()
