@@ -50,23 +50,34 @@ int va_workspace(va_context* ctx, size_t bytes, void** out) {
 
 static void prof_free(va_context* ctx);
 
-int va_io_buffer(va_context* ctx, size_t bytes, void** out) {
+static int grow_buffer(va_context* ctx, void** buf, size_t* have, size_t bytes, const char* what) {
     if (bytes == 0) bytes = 256;
-    if (ctx->io_bytes < bytes) {
-        if (ctx->io) {
+    if (*have < bytes) {
+        if (*buf) {
             VA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-            VA_CUDA_TRY(cudaFree(ctx->io));
-            ctx->io = nullptr;
-            ctx->io_bytes = 0;
+            VA_CUDA_TRY(cudaFree(*buf));
+            *buf = nullptr;
+            *have = 0;
         }
-        cudaError_t e = cudaMalloc(&ctx->io, bytes);
+        cudaError_t e = cudaMalloc(buf, bytes);
         if (e != cudaSuccess) {
-            ctx->io = nullptr;
-            return va_set_error(VA_ERR_OOM, "staging allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+            *buf = nullptr;
+            return va_set_error(VA_ERR_OOM, "%s allocation of %zu bytes failed: %s", what, bytes, cudaGetErrorString(e));
         }
-        ctx->io_bytes = bytes;
+        *have = bytes;
     }
+    return VA_OK;
+}
+
+int va_io_buffer(va_context* ctx, size_t bytes, void** out) {
+    VA_TRY(grow_buffer(ctx, &ctx->io, &ctx->io_bytes, bytes, "staging"));
     *out = ctx->io;
+    return VA_OK;
+}
+
+int va_aux_buffer(va_context* ctx, size_t bytes, void** out) {
+    VA_TRY(grow_buffer(ctx, &ctx->aux, &ctx->aux_bytes, bytes, "auxiliary scratch"));
+    *out = ctx->aux;
     return VA_OK;
 }
 
@@ -128,6 +139,7 @@ int va_context_destroy(va_context* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->io) cudaFree(ctx->io);
+    if (ctx->aux) cudaFree(ctx->aux);
     if (ctx->d_error) cudaFree(ctx->d_error);
     if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
     if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);

@@ -24,7 +24,8 @@ int db_create_impl(va_context* ctx, const void* rows, int on_device, int64_t n, 
                    uint32_t id_base, va_database** out, bool eager_operand);
 int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                              const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,
-                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n);
+                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n,
+                             uint32_t* fail_list, uint32_t* fail_cnt);
 
 namespace {
 
@@ -139,6 +140,67 @@ __global__ void k_add_base_ids(uint32_t* ids, int64_t n, uint32_t base) {
         if (ids[i] != va::kInvalidId) ids[i] += base;
 }
 
+// Exact integer L2 of SCAN_Q queries (blockIdx.y tile) against every row, on the CUDA cores
+// (dp4a): out[q * n + r] = bit pattern of |x_r|^2 + |q|^2 - 2 q.x_r as a float. The exact route
+// for queries whose wide candidate pool the filter's lists could not prove.
+constexpr int SCAN_Q = 8;
+
+__global__ void __launch_bounds__(256) k_int8_scan(const int8_t* __restrict__ qc, const int* __restrict__ qn, int nqf,
+                                                   const int8_t* __restrict__ xc, const int* __restrict__ xn, int64_t n,
+                                                   int cpad, float* __restrict__ out) {
+    extern __shared__ int4 s_q[];  // [SCAN_Q][cpad / 16]
+    const int cw = cpad / 16;
+    const int q0 = blockIdx.y * SCAN_Q;
+    const int nqt = min(SCAN_Q, nqf - q0);
+    for (int i = threadIdx.x; i < SCAN_Q * cw; i += blockDim.x) {
+        const int qq = i / cw;
+        s_q[i] = qq < nqt ? ((const int4*)(qc + (int64_t)(q0 + qq) * cpad))[i - qq * cw] : make_int4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+        int acc[SCAN_Q];
+#pragma unroll
+        for (int j = 0; j < SCAN_Q; ++j) acc[j] = 0;
+        const int4* xr = (const int4*)(xc + r * cpad);
+        for (int c = 0; c < cw; ++c) {
+            const int4 xv = __ldg(xr + c);
+#pragma unroll
+            for (int j = 0; j < SCAN_Q; ++j) {
+                const int4 qv = s_q[j * cw + c];
+                acc[j] = __dp4a(qv.x, xv.x, acc[j]);
+                acc[j] = __dp4a(qv.y, xv.y, acc[j]);
+                acc[j] = __dp4a(qv.z, xv.z, acc[j]);
+                acc[j] = __dp4a(qv.w, xv.w, acc[j]);
+            }
+        }
+        const int xnr = xn[r];
+#pragma unroll
+        for (int j = 0; j < SCAN_Q; ++j)
+            if (j < nqt) out[(int64_t)(q0 + j) * n + r] = __int_as_float(xnr + qn[q0 + j] - 2 * acc[j]);
+    }
+}
+
+__global__ void k_gather_f32_rows(const float* __restrict__ src, int dim, const uint32_t* __restrict__ rows, int64_t n,
+                                  float* __restrict__ dst) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * dim; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / dim;
+        dst[i] = src[(int64_t)rows[r] * dim + (i - r * dim)];
+    }
+}
+
+__global__ void k_scatter_rows(const float* __restrict__ v, const uint32_t* __restrict__ ids,
+                               const uint32_t* __restrict__ rows, int64_t n, int k, float* __restrict__ out_v,
+                               uint32_t* __restrict__ out_i) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * k; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / k;
+        const int64_t o = (int64_t)rows[r] * k + (i - r * k);
+        out_v[o] = v[i];
+        out_i[o] = ids[i];
+    }
+}
+
+int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8192)); }
+
 int pool_list_size(int want) {
     if (want <= 32) return 32;
     if (want <= 64) return 64;
@@ -175,8 +237,9 @@ int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntS
     return VA_OK;
 }
 
-int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s) {
+int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s, bool no_share) {
     TcFilterArgs a = {};
+    a.no_share = no_share ? 1 : 0;
     a.q_op = s.q_codes;
     a.x_op = db->codes;
     a.elem_bytes = 1;
@@ -192,6 +255,54 @@ int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, c
     a.sync_words = plan.sync_words;
     a.limit_ms = 2000u;
     return va_tc_filter(ctx, a, plan);
+}
+
+// Queries of an int8 search whose wide pool could not be proven from the filter's lists: exact
+// integer distances to every row (k_int8_scan), the `pool` best by (distance, id), the same exact
+// rerank, results written to their rows. Reads the failure count back (waits for the stream).
+int int8_fallback(va_context* ctx, va_database* db, const float* queries, int k, int pool, const uint32_t* fail_list,
+                  const uint32_t* fail_cnt, float* gq, float* gv, uint32_t* gi, float* out_vals, uint32_t* out_ids) {
+    uint32_t nf = 0;
+    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_synchronize(ctx));
+    if (!nf) return VA_OK;
+    const int dim = db->dim, cpad = db->cpad;
+    const int64_t n = db->n;
+    k_gather_f32_rows<<<grid_for((int64_t)nf * dim), 256, 0, ctx->stream>>>(queries, dim, fail_list, nf, gq);
+    VA_TRY(va_check_launch("k_gather_f32_rows"));
+    // Chunks of f queries: distances [f x n] fp32 bit patterns within 256 MiB.
+    const int64_t f_max = std::max<int64_t>(1, std::min<int64_t>((int64_t)(256ll << 20) / (4 * n), 4096));
+    const int64_t F = std::min<int64_t>(nf, f_max);
+    const size_t cb = round_up(F * cpad, 256), nb = round_up(F * 4, 256), db_ = round_up(F * n * 4, 256),
+                 lb = round_up(F * pool * 4, 256);
+    void* ws;
+    VA_TRY(va_workspace(ctx, cb + nb + db_ + 2 * lb, &ws));
+    int8_t* qc = (int8_t*)ws;
+    int* qn = (int*)((uint8_t*)ws + cb);
+    float* dist = (float*)((uint8_t*)qn + nb);
+    float* cv = (float*)((uint8_t*)dist + db_);
+    uint32_t* ci = (uint32_t*)((uint8_t*)cv + lb);
+    const size_t smem = (size_t)SCAN_Q * cpad;
+    if (smem > 48 * 1024)
+        VA_CUDA_TRY(cudaFuncSetAttribute(k_int8_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    for (int64_t c0 = 0; c0 < nf; c0 += F) {
+        const int f = (int)std::min<int64_t>(F, nf - c0);
+        const float* q = gq + c0 * dim;
+        k_perdim_codes<<<warps_grid(f), 256, 0, ctx->stream>>>(q, f, f, dim, cpad, db->sq_mins, db->sq_scales, qc, qn);
+        VA_TRY(va_check_launch("k_perdim_codes(fallback)"));
+        dim3 grid((unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)ctx->sm_count * 8), (unsigned)((f + SCAN_Q - 1) / SCAN_Q));
+        k_int8_scan<<<grid, 256, smem, ctx->stream>>>(qc, qn, f, db->codes, db->code_norms, n, cpad, dist);
+        VA_TRY(va_check_launch("k_int8_scan"));
+        VA_TRY(va_topk_select(ctx, dist, f, n, n, pool, VA_SELECT_MIN, cv, ci, pool));
+        TcPlan one = {};
+        one.splits = 1;
+        one.nq_pad = f;
+        one.kp = pool;
+        VA_TRY(va_merge_rerank_internal(ctx, db, q, f, k, VA_METRIC_L2SQ, one, cv, ci, nullptr, gv + c0 * k,
+                                        gi + c0 * k, pool, nullptr, nullptr));
+    }
+    k_scatter_rows<<<grid_for((int64_t)nf * k), 256, 0, ctx->stream>>>(gv, gi, fail_list, nf, k, out_vals, out_ids);
+    return va_check_launch("k_scatter_rows");
 }
 
 int alloc_int_db(va_context* ctx, va_database* db, int64_t n, int cpad) {
@@ -290,20 +401,47 @@ int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* que
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(k > 0, "k must be positive, got %d", k);
     VA_REQUIRE(candidates >= k, "candidates %d must be >= k %d", candidates, k);
-    const int kp = pool_list_size(candidates);
-    VA_REQUIRE(kp > 0, "candidates %d exceeds the supported pool of 128", candidates);
+    VA_REQUIRE(candidates <= VA_MAX_SELECT_K, "candidates %d exceeds the maximum of %d", candidates, VA_MAX_SELECT_K);
+    VA_REQUIRE(k <= VA_MAX_K, "k %d exceeds maximum supported k %d", k, VA_MAX_K);
+    // Up to 128 candidates: lists of that size sharing a per-query bound. More: 128-entry lists
+    // without a shared bound, the pool proven from their union per query, the rest scanned exactly.
+    const bool wide = candidates > 128;
+    const int kp = wide ? 128 : pool_list_size(candidates);
     va_database* db = const_cast<va_database*>(cdb);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     TcPlan plan;
     VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
     IntScratch s;
     VA_TRY(int_scratch(ctx, db, plan, &s));
+    uint32_t *fail_cnt = nullptr, *fail_list = nullptr, *gi = nullptr;
+    float *gq = nullptr, *gv = nullptr;
+    if (wide) {
+        void* aux;
+        const size_t lb = round_up(4 * (nq + 64), 256), qb = round_up(nq * db->dim * 4, 256),
+                     rb = round_up(nq * k * 4, 256);
+        VA_TRY(va_aux_buffer(ctx, lb + qb + 2 * rb, &aux));
+        fail_cnt = (uint32_t*)aux;
+        fail_list = fail_cnt + 64;
+        gq = (float*)((uint8_t*)aux + lb);
+        gv = (float*)((uint8_t*)gq + qb);
+        gi = (uint32_t*)((uint8_t*)gv + rb);
+        VA_CUDA_TRY(cudaMemsetAsync(fail_cnt, 0, 4, ctx->stream));
+    }
     k_perdim_codes<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, db->dim, db->cpad,
                                                                      db->sq_mins, db->sq_scales, s.q_codes, s.q_norms);
     VA_TRY(va_check_launch("k_perdim_codes(queries)"));
-    VA_TRY(run_int_filter(ctx, db, plan, s));
-    return va_merge_rerank_internal(ctx, db, queries, nq, k, VA_METRIC_L2SQ, plan, s.part_keys, s.part_ids, s.gthr,
-                                    out_vals, out_ids, candidates);
+    const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+    VA_TRY(run_int_filter(ctx, db, plan, s, wide));
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+    if (prof)
+        ctx->prof_n++;
+    else
+        ctx->k_recorded = true;
+    VA_TRY(va_merge_rerank_internal(ctx, db, queries, nq, k, VA_METRIC_L2SQ, plan, s.part_keys, s.part_ids, s.gthr,
+                                    out_vals, out_ids, candidates, fail_list, fail_cnt));
+    if (!wide) return VA_OK;
+    return int8_fallback(ctx, db, queries, k, candidates, fail_list, fail_cnt, gq, gv, gi, out_vals, out_ids);
 }
 
 int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
@@ -363,12 +501,19 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
     VA_TRY(int_scratch(ctx, db, plan, &s));
     void* ws2;
     const size_t extra = (size_t)nq * k * 8;
-    VA_TRY(va_io_buffer(ctx, extra + 256, &ws2));
+    VA_TRY(va_aux_buffer(ctx, extra + 256, &ws2));
     float* mv = (float*)ws2;
     k_expand_bits<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, db->words, db->cpad,
                                                                     s.q_codes, s.q_norms);
     VA_TRY(va_check_launch("k_expand_bits(queries)"));
-    VA_TRY(run_int_filter(ctx, db, plan, s));
+    const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+    VA_TRY(run_int_filter(ctx, db, plan, s, false));
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+    if (prof)
+        ctx->prof_n++;
+    else
+        ctx->k_recorded = true;
     VA_TRY(va_merge_lists_internal(ctx, s.part_keys, s.part_ids, plan.splits, plan.nq_pad * plan.kp, plan.kp, nq, k,
                                    VA_SELECT_MIN, mv, out_ids));
     const int blocks = std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096));

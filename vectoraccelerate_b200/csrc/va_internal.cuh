@@ -58,10 +58,16 @@ struct va_context {
     // Staging for the host-buffer entry points (queries in, results out).
     void* io = nullptr;
     size_t io_bytes = 0;
+    // Third scratch for results that must outlive the workspace within one call (gathered
+    // queries and results of the exact fallback, the Hamming merge output).
+    void* aux = nullptr;
+    size_t aux_bytes = 0;
 };
 
 // Device staging buffer of at least `bytes` for host-buffer calls.
 int va_io_buffer(va_context* ctx, size_t bytes, void** out);
+// Auxiliary device scratch of at least `bytes` (stream-ordered reuse across calls).
+int va_aux_buffer(va_context* ctx, size_t bytes, void** out);
 
 // Returns a device scratch pointer of at least `bytes` (stream-ordered reuse across calls).
 int va_workspace(va_context* ctx, size_t bytes, void** out);

@@ -117,9 +117,11 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
                                                            int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
                                                            float* __restrict__ out_vals,
-                                                           uint32_t* __restrict__ out_ids) {
+                                                           uint32_t* __restrict__ out_ids,
+                                                           uint32_t* __restrict__ fail_list,
+                                                           uint32_t* __restrict__ fail_cnt) {
     extern __shared__ uint8_t smem[];
-    const int kp2 = va::next_pow2(kp);
+    const int kp2 = va::next_pow2(max(kp, pool_n));
     uint64_t* sel = (uint64_t*)smem;       // [kp2]
     uint64_t* ex = sel + kp2;               // [kp2]
     uint64_t* pool = ex + kp2;              // [MR_POOL] candidates at or below the shared bound
@@ -161,6 +163,30 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         m = va::block_select_radix((int64_t)n_pool, pool_n, [&](int64_t i) -> uint64_t { return pool[i]; }, sel, sh);
     else
         m = va::block_select_radix(n_all, pool_n, get, sel, sh);
+    if (fail_list) {
+        // Pool wider than the lists (kp < pool_n, lists filled without a shared bound): the
+        // selection is the exact top pool_n by (key, id) when every split's list holds all of its
+        // candidates up to the selection's largest composite T, i.e. when no full list ends below
+        // T. Otherwise the query is handed to the exact fallback.
+        __shared__ unsigned long long s_t;
+        if (threadIdx.x == 0) s_t = 0;
+        __syncthreads();
+        unsigned long long t = 0;
+        for (int i = threadIdx.x; i < m; i += blockDim.x)
+            if (sel[i] != ~0ull && sel[i] > t) t = sel[i];
+        atomicMax(&s_t, t);
+        __syncthreads();
+        const unsigned long long T = s_t;
+        int bad = 0;
+        for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+            const uint64_t last = get((int64_t)s * kp + kp - 1);
+            if (last != ~0ull && last < T) bad = 1;
+        }
+        if (__syncthreads_or(bad)) {
+            if (threadIdx.x == 0) fail_list[atomicAdd(fail_cnt, 1u)] = (uint32_t)qi;
+            return;
+        }
+    }
     if (metric == VA_METRIC_COSINE && warp == 0) {
         double s = 0;
         for (int j = lane; j < dim; j += 32) s += (double)sq[j] * sq[j];
@@ -276,12 +302,66 @@ int choose_kp(int k, int rerank) {
     return 0;
 }
 
+// Pool of va_knn_search: as choose_kp up to 128; above it the wanted size itself (the filter then
+// keeps 128-entry lists without a shared bound), up to VA_MAX_SELECT_K; 0 when larger.
+int choose_pool(int k, int rerank) {
+    const int kp = choose_kp(k, rerank);
+    if (kp) return kp;
+    const int64_t want = rerank > 0 ? (int64_t)rerank * k : (int64_t)k + std::max(k / 4, 22);
+    return want <= VA_MAX_SELECT_K ? (int)want : 0;
+}
+
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids, int pool_n = 0);
+                 float* out_vals, uint32_t* out_ids, int pool_n = 0, uint32_t* fail_list = nullptr,
+                 uint32_t* fail_cnt = nullptr);
+int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, float* out_vals,
+                uint32_t* out_ids);
 
+__global__ void k_gather_rows(const float* __restrict__ src, int dim, const uint32_t* __restrict__ rows, int64_t n,
+                              float* __restrict__ dst) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * dim; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / dim;
+        dst[i] = src[(int64_t)rows[r] * dim + (i - r * dim)];
+    }
+}
+
+__global__ void k_scatter_results(const float* __restrict__ v, const uint32_t* __restrict__ ids,
+                                  const uint32_t* __restrict__ rows, int64_t n, int k, float* __restrict__ out_v,
+                                  uint32_t* __restrict__ out_i) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * k; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / k;
+        const int64_t o = (int64_t)rows[r] * k + (i - r * k);
+        out_v[o] = v[i];
+        out_i[o] = ids[i];
+    }
+}
+
+int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8192)); }
+
+// Failed queries of a wide-pool merge (fail_cnt entries of fail_list): exact FP32 search of those
+// queries, results written to their rows. Reads the count back, so the call waits for the stream.
+int fallback_exact(va_context* ctx, va_database* db, const float* queries, int k, int metric,
+                   const uint32_t* fail_list, const uint32_t* fail_cnt, float* gq, float* gv, uint32_t* gi,
+                   float* out_vals, uint32_t* out_ids) {
+    uint32_t nf = 0;
+    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_synchronize(ctx));
+    if (!nf) return VA_OK;
+    k_gather_rows<<<grid_for((int64_t)nf * db->dim), 256, 0, ctx->stream>>>(queries, db->dim, fail_list, nf, gq);
+    VA_TRY(va_check_launch("k_gather_rows"));
+    VA_TRY(search_fp32(ctx, db, gq, nf, k, metric, gv, gi));
+    k_scatter_results<<<grid_for((int64_t)nf * k), 256, 0, ctx->stream>>>(gv, gi, fail_list, nf, k, out_vals, out_ids);
+    return va_check_launch("k_scatter_results");
+}
+
+// pool <= 128: lists of the pool's size sharing a per-query bound. pool > 128: 128-entry lists
+// without a shared bound; the merge selects the pool from their union where that is provably the
+// exact top pool (see k_merge_rerank) and the remaining queries take the exact FP32 route.
 int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
-              int kp, float* out_vals, uint32_t* out_ids) {
+              int pool, float* out_vals, uint32_t* out_ids) {
+    const bool wide = pool > 128;
+    const int kp = wide ? 128 : pool;
     TcPlan plan;
     VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
     const bool cosine = metric == VA_METRIC_COSINE;
@@ -324,6 +404,25 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     a.sync_words = plan.sync_words;
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
+    a.no_share = wide ? 1 : 0;
+    // Wide pools: failure list and the fallback's gathered queries and results, sized before any
+    // kernel writes them.
+    uint32_t* fail_cnt = nullptr;
+    uint32_t* fail_list = nullptr;
+    float *gq = nullptr, *gv = nullptr;
+    uint32_t* gi = nullptr;
+    if (wide) {
+        void* aux;
+        const size_t lb = round_up(4 * (nq + 64), 256), qb = round_up(nq * db->dim * 4, 256),
+                     rb = round_up(nq * k * 4, 256);
+        VA_TRY(va_aux_buffer(ctx, lb + qb + 2 * rb, &aux));
+        fail_cnt = (uint32_t*)aux;
+        fail_list = fail_cnt + 64;
+        gq = (float*)((uint8_t*)aux + lb);
+        gv = (float*)((uint8_t*)gq + qb);
+        gi = (uint32_t*)((uint8_t*)gv + rb);
+        VA_CUDA_TRY(cudaMemsetAsync(fail_cnt, 0, 4, ctx->stream));
+    }
     const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
     VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
     VA_TRY(va_tc_filter(ctx, a, plan));
@@ -332,20 +431,24 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
         ctx->prof_n++;
     else
         ctx->k_recorded = true;
-    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
+    if (!wide) return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
+    VA_TRY(merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool,
+                        fail_list, fail_cnt));
+    return fallback_exact(ctx, db, queries, k, metric, fail_list, fail_cnt, gq, gv, gi, out_vals, out_ids);
 }
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids, int pool_n) {
-    const int kp2 = va::next_pow2(plan.kp);
+                 float* out_vals, uint32_t* out_ids, int pool_n, uint32_t* fail_list, uint32_t* fail_cnt) {
+    const int kp2 = va::next_pow2(std::max(plan.kp, pool_n));
     size_t smem = (size_t)kp2 * 16 + (size_t)MR_POOL * 8 + (size_t)db->dim * 4;
     if (smem > 48 * 1024)
         VA_CUDA_TRY(cudaFuncSetAttribute(k_merge_rerank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
                                                                     plan.kp, pool_n > 0 ? pool_n : plan.kp, queries,
                                                                     db->rows, db->dtype, db->dim,
-                                                                    metric, k, db->id_base, gthr, out_vals, out_ids);
+                                                                    metric, k, db->id_base, gthr, out_vals, out_ids,
+                                                                    fail_list, fail_cnt);
     return va_check_launch("k_merge_rerank");
 }
 
@@ -499,24 +602,28 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     VA_CUDA_TRY(cudaEventRecord(ctx->ev_start, ctx->stream));
     ctx->k_recorded = false;
-    int kp = choose_kp(k, rerank);
+    // Pools above 128 need fp32 rows: queries whose pool cannot be proven exact take the FP32 route.
+    int pool = choose_pool(k, rerank);
+    if (pool > 128 && db->dtype != VA_DTYPE_F32) pool = 0;
     int prec = precision;
     // AUTO: bf16 when the pool holds at least 3k candidates; with a thinner margin (large k) the
     // 4x smaller tf32 error keeps the true top k inside the pool; no pool size -> exact FP32 route.
-    if (prec == VA_PREC_AUTO) prec = !kp ? VA_PREC_FP32 : (kp >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
+    if (prec == VA_PREC_AUTO) prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
     if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
-        if (!kp) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
+        if (!pool) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
         prec = VA_PREC_BF16;
     }
     if (prec == VA_PREC_FP32) {
         VA_TRY(search_fp32(ctx, db, queries, nq, k, metric, out_vals, out_ids));
     } else {
-        if (!kp)
+        if (!pool)
             return va_set_error(VA_ERR_UNSUPPORTED,
-                                "candidate pool %d x k %d exceeds the tensor-core filter's 128; use precision FP32",
-                                rerank ? rerank : 3, k);
+                                "candidate pool %lld of k %d is not supported by the tensor-core route (at most %d, "
+                                "above 128 with fp32 rows); use precision FP32",
+                                (long long)(rerank ? (int64_t)rerank * k : (int64_t)k + std::max(k / 4, 22)), k,
+                                VA_MAX_SELECT_K);
         const int elem = prec == VA_PREC_TF32 ? 4 : 2;
-        VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, kp, out_vals, out_ids));
+        VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, pool, out_vals, out_ids));
     }
     VA_CUDA_TRY(cudaEventRecord(ctx->ev_stop, ctx->stream));
     return VA_OK;
@@ -668,6 +775,8 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
 // Internal entry of the merge + exact rerank step for other translation units (the int8 path).
 int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                              const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,
-                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n) {
-    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool_n);
+                             const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n,
+                             uint32_t* fail_list, uint32_t* fail_cnt) {
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool_n,
+                        fail_list, fail_cnt);
 }

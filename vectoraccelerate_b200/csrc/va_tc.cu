@@ -339,6 +339,9 @@ struct Work {
     int cpr;
     int lag;
     uint32_t* sync_cnt;  // [rounds * cpr] arrivals per chunk slot, zeroed before the launch
+    // 1: items share a per-query bound (lists hold only what can reach the final KP pool);
+    // 0: every item's list is its exact top KP by (key, id), for pools wider than KP.
+    int share;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -510,7 +513,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = load_bound(gthr + q);
+            float thr_g = w.share ? load_bound(gthr + q) : INFINITY;
             float thr = thr_g;
             // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row): lane j
             // holds columns j + 32r, r < 8; the next tile's are prefetched while this one runs.
@@ -518,7 +521,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (((t - t0) & 7) == 7) {
+                if (w.share && ((t - t0) & 7) == 7) {
                     thr_g = load_bound(gthr + q);
                     thr = fminf(thr_own, thr_g);
                 }
@@ -564,7 +567,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             {
                 // Publish this item's KP-th key (finite once the list is full) as a bound.
-                if (thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
+                if (w.share && thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
                 // The warp's 32 lists are contiguous in shared memory and in the output
                 // ([split][query][KP]): copy them with coalesced stores.
                 const int s = item / w.n_qtiles;
@@ -836,13 +839,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = load_bound(gthr + q);
+            float thr_g = w.share ? load_bound(gthr + q) : INFINITY;
             float thr = thr_g;
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (((t - t0) & 7) == 7) {
+                if (w.share && ((t - t0) & 7) == 7) {
                     thr_g = load_bound(gthr + q);
                     thr = fminf(thr_own, thr_g);
                 }
@@ -884,7 +887,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
-                if (thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
+                if (w.share && thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
                 const int s = item / w.n_qtiles;
                 const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
@@ -1042,6 +1045,7 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.cpr = p.cpr;
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
+    w.share = a.no_share ? 0 : 1;
     if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
     const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);

@@ -37,6 +37,7 @@ struct TcFilterArgs {
     uint32_t* sync_cnt;     // [sync_words] pacing counters, zeroed by va_tc_filter
     int64_t sync_words;
     unsigned limit_ms;    // bound of every device-side wait
+    int no_share;         // 1: no shared bound; each split's list is its exact top kp by (key, id)
 };
 
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
