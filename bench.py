@@ -56,7 +56,36 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=1_000_000, help="database rows of the CPU sample")
     p.add_argument("--no-clocks", action="store_true")
-    return p.parse_args()
+    p.add_argument("--config", choices=["headline"] + sorted(CONFIGS), default="headline",
+                   help="headline (the default bench line) or one of the other BASELINE configurations")
+    a = p.parse_args()
+    if a.config != "headline":
+        # the other configurations carry their own sizes unless given explicitly
+        c = CONFIGS[a.config]
+        for key in ("n", "dim", "nq", "k"):
+            if getattr(a, key) == p.get_default(key):
+                setattr(a, key, c[key])
+    return a
+
+
+# Other BASELINE configurations (seeded synthetic stand-ins, generated on the device). Mixture rows:
+# centroid c (TestRNG, seed ^ const, stream c) + sigma * N(0,1) (seed, stream = row), optionally
+# unit-normalised; queries come from the same mixture on streams offset by 2^31.
+CONFIGS = {
+    "c2": dict(desc="flat cosine k-NN, mixture of 1,024 centroids sigma 0.3, L2-normalised",
+               n=1_000_000, dim=1536, nq=10_000, k=100, kind="float", metric="COSINE", rows="f32",
+               mixture=(1024, 0.3, True), rerank=0),
+    "c3": dict(desc="sharded flat max-inner-product k-NN, bf16 rows, mixture of 4,096 centroids sigma 0.25, "
+                    "normalised; exact rerank of the top 4k", n=50_000_000, dim=768, nq=4096, k=10, kind="float",
+               metric="IP", rows="bf16", mixture=(4096, 0.25, True), rerank=4),
+    "c4": dict(desc="int8 scalar-quantized L2 k-NN (per-dimension min/max over the database), mixture of 2,048 "
+                    "centroids sigma 0.3; int32 L2 on codes, exact fp32-row rerank of the top 1,000",
+               n=20_000_000, dim=768, nq=8192, k=100, kind="int8", mixture=(2048, 0.3, False), candidates=1000),
+    "c5": dict(desc="Hamming k-NN over sign bits of N(0,1) d=1024 (database seed 2, queries seed 3)",
+               n=200_000_000, dim=1024, nq=1024, k=100, kind="binary"),
+    "c5q1": dict(desc="Hamming k-NN, single query (latency), sign bits of N(0,1) d=1024 (seeds 2 / 3)",
+                 n=200_000_000, dim=1024, nq=1, k=100, kind="binary"),
+}
 
 
 def workload(a):
@@ -351,10 +380,257 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------ other configs
+def auto_precision(k: int, rerank: int, f32_rows: bool = True) -> str:
+    """The filter precision va_knn_search picks under PREC_AUTO: bf16 when the candidate pool
+    (rerank * k, else k + max(k/4, 22), rounded up to 32/64/128 when it fits) holds >= 3k, and,
+    without a caller's factor, over fp32 rows (the pool then widens to 3k)."""
+    want = rerank * k if rerank else k + max(k // 4, 22)
+    pool = next((p for p in (32, 64, 128) if want <= p), want)
+    if pool < 3 * k and rerank == 0 and f32_rows and 3 * k <= 4096:
+        return "bf16"
+    return "bf16" if pool >= 3 * k else "tf32"
+
+
+def run_config(a):
+    """One of the other BASELINE configurations on this rank's row shard (N/world rows, global
+    ids = shard base + row), all-gather + device merge for world > 1, as the headline."""
+    import torch
+    import torch.distributed as dist
+
+    import vectoraccelerate_b200 as va
+    from vectoraccelerate_b200 import _ffi
+    from vectoraccelerate_b200.sharded import ShardedSearch, device_merge, shard_bounds
+
+    c = CONFIGS[a.config]
+    kind = c["kind"]
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
+    n_total = a.n
+    note = None
+    if kind == "binary" and world == 1 and a.nq > 8 and n_total > 100_000_000:
+        # the tensor-core route holds the 0/1 expansion (1 KB per 1024-bit row): 200M rows need
+        # two GPUs; one GPU takes half the database
+        n_total = 100_000_000
+        note = "1 GPU: N = 100M (the 0/1 expansion of 200M codes exceeds one GPU's HBM); N = 200M from 2 GPUs"
+    row0, n_local = shard_bounds(n_total, world, rank)
+    dim, nq, k = a.dim, a.nq, a.k
+    chunk = max(1, (4 << 30) // (4 * dim))  # fp32 generation chunks of <= 4 GiB
+
+    def gen_f32(dst_ptr, rows, seed, r0):
+        if c.get("mixture"):
+            nc, sigma, norm = c["mixture"]
+            _ffi.call("va_gen_mixture", ctx.handle, dst_ptr, rows, dim, seed, r0, nc, sigma, int(norm))
+        else:
+            _ffi.call("va_gen_gaussian", ctx.handle, dst_ptr, rows, dim, seed, r0)
+
+    db_seed, q_seed, q_row0 = (2, 3, 0) if kind == "binary" else (0, 0, QUERY_ROW0)
+    # ---- database shard
+    if kind == "float" and c["rows"] == "bf16":
+        rows = torch.empty((n_local, dim), dtype=torch.int16, device="cuda")
+        tmp = torch.empty((min(chunk, n_local), dim), dtype=torch.float32, device="cuda")
+        for r in range(0, n_local, chunk):
+            m = min(chunk, n_local - r)
+            gen_f32(tmp.data_ptr(), m, db_seed, row0 + r)
+            _ffi.call("va_f32_to_bf16", ctx.handle, tmp.data_ptr(), m * dim, rows[r:r + m].data_ptr())
+        ctx.synchronize()
+        del tmp
+        torch.cuda.empty_cache()
+        db = va.Database(ctx, None, dtype=va.DTYPE_BF16, device_ptr=rows.data_ptr(), n=n_local, dim=dim,
+                         id_base=row0)
+    elif kind in ("float", "int8"):
+        rows = torch.empty((n_local, dim), dtype=torch.float32, device="cuda")
+        for r in range(0, n_local, chunk):
+            gen_f32(rows[r:].data_ptr(), min(chunk, n_local - r), db_seed, row0 + r)
+        ctx.synchronize()
+        if kind == "float":
+            db = va.Database(ctx, None, device_ptr=rows.data_ptr(), n=n_local, dim=dim, id_base=row0)
+        else:
+            # per-dimension range over the WHOLE database: local min / max, then MIN / MAX all-reduce
+            mn = torch.empty(dim, dtype=torch.float32, device="cuda")
+            mx = torch.empty(dim, dtype=torch.float32, device="cuda")
+            _ffi.call("va_sq_perdim_minmax", ctx.handle, rows.data_ptr(), n_local, dim, mn.data_ptr(), mx.data_ptr())
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+                dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            db = va.Int8Database(ctx, None, id_base=row0, mins=mn.cpu().numpy(), maxs=mx.cpu().numpy(),
+                                 device_ptr=rows.data_ptr(), n=n_local, dim=dim)
+    else:
+        words = dim // 32
+        rows = torch.empty((n_local, words), dtype=torch.int32, device="cuda")
+        tmp = torch.empty((min(chunk, n_local), dim), dtype=torch.float32, device="cuda")
+        for r in range(0, n_local, chunk):
+            m = min(chunk, n_local - r)
+            gen_f32(tmp.data_ptr(), m, db_seed, row0 + r)
+            _ffi.call("va_binary_quantize", ctx.handle, tmp.data_ptr(), m, dim, 0.0, rows[r:r + m].data_ptr())
+        ctx.synchronize()
+        del tmp
+        db = va.BinaryDatabase.from_device(ctx, rows.data_ptr(), n_local, dim, id_base=row0)
+    ctx.synchronize()
+    del rows
+    torch.cuda.empty_cache()
+
+    # ---- queries (device copy for `value`, pinned host copy for `e2e`)
+    if kind == "binary":
+        qf = torch.empty((nq, dim), dtype=torch.float32, device="cuda")
+        gen_f32(qf.data_ptr(), nq, q_seed, q_row0)
+        dq = torch.empty((nq, dim // 32), dtype=torch.int32, device="cuda")
+        _ffi.call("va_binary_quantize", ctx.handle, qf.data_ptr(), nq, dim, 0.0, dq.data_ptr())
+        del qf
+    else:
+        dq = torch.empty((nq, dim), dtype=torch.float32, device="cuda")
+        gen_f32(dq.data_ptr(), nq, q_seed, q_row0)
+    ctx.synchronize()
+    hq = dq.cpu().pin_memory()
+    lv = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    li = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    hv = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    hi = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    metric = {"COSINE": va.METRIC_COSINE, "IP": va.METRIC_IP}.get(c.get("metric"), va.METRIC_L2SQ)
+    mode = 1 if metric == va.METRIC_IP and kind == "float" else 0
+
+    def local_search(nq_, kk):
+        if kind == "float":
+            _ffi.call("va_knn_search", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, metric, va.PREC_AUTO,
+                      c["rerank"], lv.data_ptr(), li.data_ptr())
+        elif kind == "int8":
+            _ffi.call("va_int8_knn_search", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, c["candidates"],
+                      lv.data_ptr(), li.data_ptr())
+        else:
+            # uint32 distances are written as their bit patterns into the float list; those order
+            # like the integers, so the float merge applies unchanged
+            _ffi.call("va_hamming_knn_db", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, lv.data_ptr(),
+                      li.data_ptr())
+        return lv, li
+
+    sharded = ShardedSearch(world, local_search, device_merge(ctx, world, nq, k, mode=mode))
+    final = [lv, li]
+
+    def step():
+        final[0], final[1] = sharded.search(nq, k)
+
+    def step_e2e():
+        dq.copy_(hq, non_blocking=True)
+        step()
+        hv.copy_(final[0], non_blocking=True)
+        hi.copy_(final[1], non_blocking=True)
+
+    def barrier_sync():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    barrier_sync()
+    ids0 = final[1].cpu().numpy().view(np.uint32)
+    assert (ids0 < n_total).all(), "search returned invalid ids"
+
+    clocks = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else "0",
+                          enabled=(rank == 0 and not a.no_clocks))
+    _ffi.call("va_profile_start", ctx.handle, a.steps)
+    barrier_sync()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    barrier_sync()
+    clk = clocks.stop()
+    per = sorted(e0.elapsed_time(e1) for e0, e1 in evs)
+    ms = max_over_ranks(float(np.mean(per)))
+    p50 = max_over_ranks(per[len(per) // 2])
+    p99 = max_over_ranks(per[min(len(per) - 1, int(round(0.99 * (len(per) - 1))))])
+    kms, kcalls = ctypes.c_float(), ctypes.c_int()
+    _ffi.call("va_profile_stop", ctx.handle, ctypes.byref(kms), ctypes.byref(kcalls))
+    kernel_ms = max_over_ranks(kms.value / max(1, kcalls.value)) if kcalls.value else None
+
+    for _ in range(a.warmup):
+        step_e2e()
+    barrier_sync()
+    e0, e1 = evs[0]
+    e0.record(stream)
+    for _ in range(a.steps):
+        step_e2e()
+    e1.record(stream)
+    barrier_sync()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peaks, peak_src = measured_peaks()
+    bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    roof = None
+    if kernel_ms:
+        if kind == "binary" and nq <= 8:
+            byts = n_local * dim / 8.0
+            ach = byts / (kernel_ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": ach / peaks["hbm_gbs"], "traffic": None, "kernel": "k_hamming_scan",
+                    "kernel_ms": kernel_ms, "bytes_per_launch": byts,
+                    "peak_source": f"{peak_src} HBM copy bandwidth"}
+        else:
+            ops = 2.0 * nq * n_local * dim
+            if kind == "float":
+                peak, lab, unit = bf16, f"{peak_src} bf16 sustained", "TFLOP/s"
+                prec_used = auto_precision(k, c["rerank"], c["rows"] == "f32")
+                if prec_used == "tf32":
+                    peak, lab = bf16 / 2.0, f"{peak_src} bf16 sustained / 2 for tf32"
+            else:
+                prec_used = "int8"
+                peak, lab, unit = 2.0 * bf16, f"2 x {peak_src} bf16 sustained (dense int8 rate = 2 x bf16)", "TOP/s"
+            ach = ops / (kernel_ms * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
+                    "traffic": None, "kernel": "k_tc_filter", "kernel_ms": kernel_ms, "ops_per_launch": ops,
+                    "filter_precision": prec_used, "peak_source": lab}
+    in_bytes = hq.numel() * hq.element_size()
+    line = {
+        "metric": f"queries/sec, {a.config}: {c['desc']}", "value": nq / (ms * 1e-3), "unit": "queries/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": {"float": "bf16/tf32 filter + f64 exact rerank", "int8": "s8 codes, s32 accumulate + f64 rerank",
+                  "binary": "u1 codes (popcount / s8 0-1 tensor-core contraction)"}[kind],
+        "data": "synthetic: TestRNG restatement on the device", "config": {
+            "workload": c["desc"], "config": a.config, "N": n_total, "d": dim, "Q": nq, "k": k,
+            "parallelism": f"row-shard x{world}, NCCL allgather + device merge",
+            "l2_policy": "inputs larger than L2, no flush"},
+        "latency_ms": {"p50": p50, "p99": p99},
+        "e2e": {"value": nq / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": world * in_bytes,
+                "d2h_bytes_per_step": world * nq * k * 8},
+        "roofline": roof, "clocks": clk,
+    }
+    if note:
+        line["note"] = note
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     a = parse_args()
     if a.impl == "reference":
         run_reference(a)
+    elif a.config != "headline":
+        run_config(a)
     else:
         run_ours(a)
 

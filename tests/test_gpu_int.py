@@ -130,3 +130,44 @@ def test_hamming_db_duplicates_and_base(ctx, oracle):
         db.close()
     assert np.array_equal(gd, od)
     assert np.array_equal(gi - np.uint32(7), oi)
+
+
+@pytest.mark.parametrize("n,bits,nq,k", [
+    (200_000, 1024, 1, 100),
+    (200_000, 1024, 8, 100),
+    (50_000, 512, 3, 128),
+    (50_000, 256, 5, 1),
+    (30_001, 128, 2, 64),
+    (5003, 96, 1, 10),      # 3 words: no packed scan, the expanded tensor-core route
+])
+def test_hamming_db_small_batch(ctx, oracle, n, bits, nq, k):
+    """Small batches take the HBM-bound scan over the packed codes."""
+    import vectoraccelerate_b200 as va
+    x = oracle.binary_quantize(oracle.gen_gaussian(n, bits, 2))
+    q = oracle.binary_quantize(oracle.gen_gaussian(nq, bits, 3, row0=QROW))
+    oi, od = oracle.hamming_knn(q, x, k)
+    db = va.BinaryDatabase(ctx, x, bits, id_base=11)
+    try:
+        gd, gi = db.search(q, k)
+    finally:
+        db.close()
+    assert np.array_equal(gd, od)
+    assert np.array_equal(gi - np.uint32(11), oi)
+
+
+def test_hamming_db_small_batch_ties(ctx, oracle):
+    """Every code 300 times in a row: distance-0 runs force repeated buffer compactions; the
+    (distance, id) order must survive them."""
+    import vectoraccelerate_b200 as va
+    base = oracle.binary_quantize(oracle.gen_gaussian(200, 1024, 5))
+    x = np.repeat(base, 300, axis=0)
+    q = base[[3, 150, 199]].copy()
+    oi, od = oracle.hamming_knn(q, x, 128)
+    db = va.BinaryDatabase(ctx, x, 1024)
+    try:
+        gd, gi = db.search(q, 128)
+        gd1, gi1 = db.search(q[:1], 128)
+    finally:
+        db.close()
+    assert np.array_equal(gd, od) and np.array_equal(gi, oi)
+    assert np.array_equal(gd1, od[:1]) and np.array_equal(gi1, oi[:1])

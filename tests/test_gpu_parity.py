@@ -359,14 +359,15 @@ def test_pair_kernel_parity(oracle, c1, tmp_path):
         assert frac >= 0.999
 
 
-@pytest.mark.parametrize("metric,n,d,k", [(1, 30_000, 1536, 100), (0, 40_000, 768, 50), (2, 25_000, 256, 100),
-                                          (0, 20_000, 128, 42)],
-                         ids=["cos-k100-d1536", "l2-k50", "ip-k100", "l2-k42"])
-def test_fused_large_k(ctx, oracle, metric, n, d, k):
-    """Pools of 64/128 candidates (k up to 106) on the tensor-core route; auto precision picks
-    tf32 when the pool is thinner than 3k."""
+@pytest.mark.parametrize("metric,n,d,k,prec", [(1, 30_000, 1536, 100, 0), (0, 40_000, 768, 50, 0),
+                                               (2, 25_000, 256, 100, 0), (0, 20_000, 128, 42, 0),
+                                               (1, 30_000, 1536, 100, 2), (2, 25_000, 256, 100, 2)],
+                         ids=["cos-k100-d1536", "l2-k50", "ip-k100", "l2-k42", "cos-k100-tf32", "ip-k100-tf32"])
+def test_fused_large_k(ctx, oracle, metric, n, d, k, prec):
+    """Large k on the tensor-core route. Auto precision over fp32 rows: bf16 with a 3k pool
+    (wider than the 128-entry lists from k = 43 on); explicit TF32: the k + max(k/4, 22) pool."""
     x = oracle.gen_mixture(n, d, 31, 64, 0.3, metric == 1)
     q = oracle.gen_mixture(96, d, 32, 64, 0.3, metric == 1)
-    vals, ids = _knn(ctx, x, q, k, metric=metric)
+    vals, ids = _knn(ctx, x, q, k, metric=metric, precision=prec)
     frac = _check(oracle, q, x, k, metric, vals, ids)
     assert frac >= 0.999

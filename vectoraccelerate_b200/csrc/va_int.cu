@@ -201,6 +201,136 @@ __global__ void k_scatter_rows(const float* __restrict__ v, const uint32_t* __re
 
 int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8192)); }
 
+// ------------------------------------------------------------------------------------------------
+// Small-batch Hamming scan (NQ <= 8 queries): one streaming pass over the PACKED codes, which is
+// HBM-bound (128 B per 1024-bit row) where the tensor-core route would read the 8x larger 0/1
+// expansion. LPR = WORDS/4 lanes hold one row (16 B each, coalesced); popcounts are reduced over
+// those lanes. Each CTA keeps, per query, a shared-memory buffer of (distance << 32 | row)
+// composites below its running threshold (the k-th best composite after the last compaction);
+// when a buffer could overflow in the next iteration, a block-wide radix selection compacts it to
+// the k best. Each CTA writes its k best per query; a merge over CTAs gives the result.
+constexpr int HS_THREADS = 256;
+constexpr int HS_BUF = 1024;  // composites per query buffer
+
+template <int WORDS, int NQ>
+__global__ void __launch_bounds__(HS_THREADS) k_hamming_scan(const uint32_t* __restrict__ x, int64_t n,
+                                                             const uint32_t* __restrict__ q, int nq, int k,
+                                                             int64_t rows_per_cta, float* __restrict__ part_vals,
+                                                             uint32_t* __restrict__ part_ids) {
+    constexpr int LPR = WORDS / 4;               // lanes per row
+    constexpr int RPW = 32 / LPR;                // rows per warp load
+    // Loads in flight per lane; an iteration covers at most 512 rows, so a buffer compacted to
+    // <= 128 entries (or holding <= HS_BUF - IROWS) cannot overflow in the next one.
+    constexpr int HS_UNROLL = WORDS / 2 < 8 ? WORDS / 2 : 8;
+    constexpr int WROWS = RPW * HS_UNROLL;       // rows per warp per iteration
+    constexpr int IROWS = WROWS * (HS_THREADS / 32);
+    static_assert(IROWS + 128 <= HS_BUF && IROWS <= HS_BUF / 2, "buffer too small for one iteration");
+    extern __shared__ uint64_t s_buf[];          // [NQ][HS_BUF]
+    __shared__ uint64_t s_tmp[128];
+    __shared__ unsigned long long s_thr[NQ];
+    __shared__ int s_cnt[NQ];
+    __shared__ va::SelectShared sh;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sub = lane % LPR, rsub = lane / LPR;
+    uint4 qv[NQ];
+#pragma unroll
+    for (int j = 0; j < NQ; ++j)
+        qv[j] = j < nq ? ((const uint4*)(q + (int64_t)j * WORDS))[sub] : make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < NQ) {
+        s_thr[threadIdx.x] = ~0ull;
+        s_cnt[threadIdx.x] = 0;
+    }
+    __syncthreads();
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    const int64_t r1 = min(n, r0 + rows_per_cta);
+
+    // Compact query j's buffer to its k best composites (block-wide; all threads call).
+    auto compact = [&](int j) {
+        const int c = min(s_cnt[j], HS_BUF);
+        uint64_t* b = s_buf + (size_t)j * HS_BUF;
+        const int m = va::block_select_radix((int64_t)c, k, [&](int64_t i) -> uint64_t { return b[i]; }, s_tmp, sh);
+        __syncthreads();
+        for (int i = threadIdx.x; i < m; i += blockDim.x) b[i] = s_tmp[i];
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            s_cnt[j] = m;
+            if (m == k) {
+                unsigned long long t = 0;
+                for (int i = 0; i < m; ++i) t = b[i] > t ? b[i] : t;
+                s_thr[j] = t;
+            }
+        }
+        __syncthreads();
+    };
+
+    for (int64_t base = r0; base < r1; base += IROWS) {
+        const int64_t wbase = base + (int64_t)warp * WROWS;
+        uint4 v[HS_UNROLL];
+#pragma unroll
+        for (int u = 0; u < HS_UNROLL; ++u) {
+            const int64_t row = wbase + u * RPW + rsub;
+            v[u] = row < r1 ? __ldcs((const uint4*)(x + row * WORDS) + sub) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < HS_UNROLL; ++u) {
+            const int64_t row = wbase + u * RPW + rsub;
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                uint32_t d = __popc(v[u].x ^ qv[j].x) + __popc(v[u].y ^ qv[j].y) + __popc(v[u].z ^ qv[j].z) +
+                             __popc(v[u].w ^ qv[j].w);
+#pragma unroll
+                for (int o = 1; o < LPR; o <<= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+                const uint64_t comp = ((uint64_t)d << 32) | (uint64_t)(uint32_t)row;
+                if (sub == 0 && j < nq && row < r1 && comp < s_thr[j]) {
+                    const int slot = atomicAdd(&s_cnt[j], 1);
+                    if (slot < HS_BUF) s_buf[(size_t)j * HS_BUF + slot] = comp;
+                }
+            }
+        }
+        __syncthreads();
+        // A buffer that the next iteration could overflow is compacted now (uniform decision).
+        for (int j = 0; j < nq; ++j)
+            if (s_cnt[j] > HS_BUF - IROWS) compact(j);
+    }
+    for (int j = 0; j < nq; ++j) {
+        compact(j);
+        const int m = s_cnt[j];
+        float* pv = part_vals + ((int64_t)blockIdx.x * nq + j) * k;
+        uint32_t* pi = part_ids + ((int64_t)blockIdx.x * nq + j) * k;
+        for (int i = threadIdx.x; i < k; i += blockDim.x) {
+            const uint64_t c = i < m ? s_buf[(size_t)j * HS_BUF + i] : ~0ull;
+            pv[i] = c == ~0ull ? INFINITY : __uint_as_float((uint32_t)(c >> 32));
+            pi[i] = c == ~0ull ? va::kInvalidId : (uint32_t)c;
+        }
+        __syncthreads();
+    }
+}
+
+template <int WORDS, int NQ>
+int launch_hscan(va_context* ctx, const uint32_t* x, int64_t n, const uint32_t* q, int nq, int k, int grid,
+                 int64_t rows_per_cta, float* pv, uint32_t* pi) {
+    const size_t smem = (size_t)NQ * HS_BUF * 8;
+    if (smem > 48 * 1024)
+        VA_CUDA_TRY(cudaFuncSetAttribute(k_hamming_scan<WORDS, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_hamming_scan<WORDS, NQ><<<grid, HS_THREADS, smem, ctx->stream>>>(x, n, q, nq, k, rows_per_cta, pv, pi);
+    return va_check_launch("k_hamming_scan");
+}
+
+template <int WORDS>
+int dispatch_hscan(va_context* ctx, const uint32_t* x, int64_t n, const uint32_t* q, int nq, int k, int grid,
+                   int64_t rows_per_cta, float* pv, uint32_t* pi) {
+    if (nq <= 1) return launch_hscan<WORDS, 1>(ctx, x, n, q, nq, k, grid, rows_per_cta, pv, pi);
+    if (nq <= 2) return launch_hscan<WORDS, 2>(ctx, x, n, q, nq, k, grid, rows_per_cta, pv, pi);
+    if (nq <= 4) return launch_hscan<WORDS, 4>(ctx, x, n, q, nq, k, grid, rows_per_cta, pv, pi);
+    return launch_hscan<WORDS, 8>(ctx, x, n, q, nq, k, grid, rows_per_cta, pv, pi);
+}
+
+constexpr int HS_MAX_Q = 8;
+
+bool hscan_supported(int words, int64_t nq) {
+    return nq <= HS_MAX_Q && (words == 4 || words == 8 || words == 16 || words == 32);
+}
+
 int pool_list_size(int want) {
     if (want <= 32) return 32;
     if (want <= 64) return 64;
@@ -222,8 +352,8 @@ struct IntScratch {
 int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntScratch* s) {
     const size_t qb = (size_t)plan.nq_pad * db->cpad;
     const size_t part = (size_t)plan.splits * plan.nq_pad * plan.kp;
-    const size_t bytes = round_up((int64_t)qb, 256) + (size_t)plan.nq_pad * 4 + part * 8 + (size_t)plan.nq_pad * 4 +
-                         (size_t)plan.sync_words * 4 + 512;
+    const size_t bytes = round_up((int64_t)qb, 256) + (size_t)plan.nq_pad * 4 + part * 8 +
+                         (size_t)plan.bound_slots * plan.nq_pad * 4 + (size_t)plan.sync_words * 4 + 512;
     void* ws;
     VA_TRY(va_workspace(ctx, bytes, &ws));
     uint8_t* p = (uint8_t*)ws;
@@ -233,13 +363,13 @@ int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntS
     s->part_keys = (float*)(s->q_norms + plan.nq_pad);
     s->part_ids = (uint32_t*)(s->part_keys + part);
     s->gthr = s->part_ids + part;
-    s->sync = s->gthr + plan.nq_pad;
+    s->sync = s->gthr + (size_t)plan.bound_slots * plan.nq_pad;
     return VA_OK;
 }
 
-int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s, bool no_share) {
+int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s) {
     TcFilterArgs a = {};
-    a.no_share = no_share ? 1 : 0;
+    a.bound_slots = plan.bound_slots;
     a.q_op = s.q_codes;
     a.x_op = db->codes;
     a.elem_bytes = 1;
@@ -406,11 +536,10 @@ int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* que
     // Up to 128 candidates: lists of that size sharing a per-query bound. More: 128-entry lists
     // without a shared bound, the pool proven from their union per query, the rest scanned exactly.
     const bool wide = candidates > 128;
-    const int kp = wide ? 128 : pool_list_size(candidates);
     va_database* db = const_cast<va_database*>(cdb);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     TcPlan plan;
-    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, candidates, &plan));
     IntScratch s;
     VA_TRY(int_scratch(ctx, db, plan, &s));
     uint32_t *fail_cnt = nullptr, *fail_list = nullptr, *gi = nullptr;
@@ -432,7 +561,7 @@ int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* que
     VA_TRY(va_check_launch("k_perdim_codes(queries)"));
     const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
     VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
-    VA_TRY(run_int_filter(ctx, db, plan, s, wide));
+    VA_TRY(run_int_filter(ctx, db, plan, s));
     VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
     if (prof)
         ctx->prof_n++;
@@ -472,12 +601,6 @@ int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, i
     e = cudaMemcpyAsync(db->rows, codes, pbytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                         ctx->stream);
     if (e != cudaSuccess) s = va_set_error(VA_ERR_CUDA, "code upload failed: %s", cudaGetErrorString(e));
-    if (s == VA_OK) s = alloc_int_db(ctx, db, n, db->cpad);
-    if (s == VA_OK) {
-        k_expand_bits<<<warps_grid(n), 256, 0, ctx->stream>>>((const uint32_t*)db->rows, n, n, db->words, db->cpad,
-                                                             db->codes, db->code_norms);
-        s = va_check_launch("k_expand_bits");
-    }
     if (s != VA_OK) {
         va_db_destroy(db);
         return s;
@@ -494,6 +617,51 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
     VA_REQUIRE(k > 0 && k <= 128, "k must be between 1 and 128 for the binary search, got %d", k);
     va_database* db = const_cast<va_database*>(cdb);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    const int blocks = std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096));
+    if (hscan_supported(db->words, nq)) {
+        // Small batch: one HBM-bound pass over the packed codes.
+        const int64_t n = db->n;
+        int grid = ctx->sm_count * 3;
+        int64_t rpc = (n + grid - 1) / grid;
+        rpc = round_up(rpc, 256);
+        grid = (int)((n + rpc - 1) / rpc);
+        const size_t part = (size_t)grid * nq * k;
+        void* ws;
+        VA_TRY(va_workspace(ctx, part * 8 + 256, &ws));
+        float* pv = (float*)ws;
+        uint32_t* pi = (uint32_t*)(pv + part);
+        void* ws2;
+        VA_TRY(va_aux_buffer(ctx, (size_t)nq * k * 4 + 256, &ws2));
+        float* mv = (float*)ws2;
+        const uint32_t* x = (const uint32_t*)db->rows;
+        const int qn = (int)nq;
+        const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+        VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+        int st;
+        switch (db->words) {
+            case 4: st = dispatch_hscan<4>(ctx, x, n, queries, qn, k, grid, rpc, pv, pi); break;
+            case 8: st = dispatch_hscan<8>(ctx, x, n, queries, qn, k, grid, rpc, pv, pi); break;
+            case 16: st = dispatch_hscan<16>(ctx, x, n, queries, qn, k, grid, rpc, pv, pi); break;
+            default: st = dispatch_hscan<32>(ctx, x, n, queries, qn, k, grid, rpc, pv, pi); break;
+        }
+        VA_TRY(st);
+        VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+        if (prof)
+            ctx->prof_n++;
+        else
+            ctx->k_recorded = true;
+        VA_TRY(va_merge_lists_internal(ctx, pv, pi, grid, nq * k, k, nq, k, VA_SELECT_MIN, mv, out_ids));
+        if (out_dists) k_bits_to_dists<<<blocks, 256, 0, ctx->stream>>>(mv, out_ids, nq * k, out_dists);
+        if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
+        return va_check_launch("k_bits_to_dists");
+    }
+    // Batches: the 0/1 expansion of the codes (built on first use) on the integer tensor cores.
+    if (!db->codes) {
+        VA_TRY(alloc_int_db(ctx, db, db->n, db->cpad));
+        k_expand_bits<<<warps_grid(db->n), 256, 0, ctx->stream>>>((const uint32_t*)db->rows, db->n, db->n, db->words,
+                                                                 db->cpad, db->codes, db->code_norms);
+        VA_TRY(va_check_launch("k_expand_bits"));
+    }
     const int kp = pool_list_size(k);
     TcPlan plan;
     VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
@@ -508,7 +676,7 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
     VA_TRY(va_check_launch("k_expand_bits(queries)"));
     const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
     VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
-    VA_TRY(run_int_filter(ctx, db, plan, s, false));
+    VA_TRY(run_int_filter(ctx, db, plan, s));
     VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
     if (prof)
         ctx->prof_n++;
@@ -516,7 +684,6 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
         ctx->k_recorded = true;
     VA_TRY(va_merge_lists_internal(ctx, s.part_keys, s.part_ids, plan.splits, plan.nq_pad * plan.kp, plan.kp, nq, k,
                                    VA_SELECT_MIN, mv, out_ids));
-    const int blocks = std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096));
     if (out_dists) k_bits_to_dists<<<blocks, 256, 0, ctx->stream>>>(mv, out_ids, nq * k, out_dists);
     if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
     return va_check_launch("k_bits_to_dists");

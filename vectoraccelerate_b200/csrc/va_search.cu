@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
                                                            const float* __restrict__ queries,
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
                                                            int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
+                                                           int nslots,
                                                            float* __restrict__ out_vals,
                                                            uint32_t* __restrict__ out_ids,
                                                            uint32_t* __restrict__ fail_list,
@@ -140,12 +141,13 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         if (id == va::kInvalidId) return ~0ull;
         return va::composite(va::f2key(part_keys[off]), id);
     };
-    // The filter's shared bound (smallest KP-th key any work item published for this query) is
-    // at least the global KP-th key, so candidates above it cannot be in the pool: one pass keeps
-    // the rest in shared memory and the selection runs there. If more than MR_POOL survive, the
-    // selection runs over all candidates instead.
+    // The filter's shared bound (the largest of its nslots slots, each the smallest KP-th key
+    // published by the items of that slot) is at least the global pool_n-th key, so candidates
+    // above it cannot be in the pool: one pass keeps the rest in shared memory and the selection
+    // runs there. If more than MR_POOL survive, the selection runs over all candidates instead.
     const int64_t n_all = (int64_t)splits * kp;
-    const uint32_t bound = gthr ? gthr[qi] : 0xFFFFFFFFu;
+    uint32_t bound = gthr ? 0u : 0xFFFFFFFFu;
+    for (int sl = 0; gthr && sl < nslots; ++sl) bound = max(bound, gthr[(int64_t)sl * nq_pad + qi]);
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < n_all; i += blockDim.x) {
@@ -361,17 +363,17 @@ int fallback_exact(va_context* ctx, va_database* db, const float* queries, int k
 int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
               int pool, float* out_vals, uint32_t* out_ids) {
     const bool wide = pool > 128;
-    const int kp = wide ? 128 : pool;
     TcPlan plan;
-    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, pool, &plan));
+    const int kp = plan.kp;  // list length (up to 128 the whole list is the pool)
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = nullptr;
     VA_TRY(ensure_operand(ctx, db, elem, cosine, &x_op));
     // Scratch: query operand, partial lists, shared per-query bounds.
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
-    const size_t bytes =
-        round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + (size_t)plan.sync_words * 4 + 256;
+    const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.bound_slots * plan.nq_pad * 4 +
+                         (size_t)plan.sync_words * 4 + 256;
     void* ws;
     VA_TRY(va_workspace(ctx, bytes, &ws));
     uint8_t* p = (uint8_t*)ws;
@@ -380,7 +382,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     float* part_keys = (float*)p;
     uint32_t* part_ids = (uint32_t*)(part_keys + part);
     uint32_t* gthr = part_ids + part;
-    uint32_t* sync_cnt = gthr + plan.nq_pad;
+    uint32_t* sync_cnt = gthr + (size_t)plan.bound_slots * plan.nq_pad;
     if (elem == 2)
         k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
@@ -404,7 +406,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     a.sync_words = plan.sync_words;
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
-    a.no_share = wide ? 1 : 0;
+    a.bound_slots = plan.bound_slots;
     // Wide pools: failure list and the fallback's gathered queries and results, sized before any
     // kernel writes them.
     uint32_t* fail_cnt = nullptr;
@@ -447,7 +449,8 @@ int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
                                                                     plan.kp, pool_n > 0 ? pool_n : plan.kp, queries,
                                                                     db->rows, db->dtype, db->dim,
-                                                                    metric, k, db->id_base, gthr, out_vals, out_ids,
+                                                                    metric, k, db->id_base, gthr,
+                                                                    std::max(1, plan.bound_slots), out_vals, out_ids,
                                                                     fail_list, fail_cnt);
     return va_check_launch("k_merge_rerank");
 }
@@ -606,9 +609,15 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     int pool = choose_pool(k, rerank);
     if (pool > 128 && db->dtype != VA_DTYPE_F32) pool = 0;
     int prec = precision;
-    // AUTO: bf16 when the pool holds at least 3k candidates; with a thinner margin (large k) the
-    // 4x smaller tf32 error keeps the true top k inside the pool; no pool size -> exact FP32 route.
-    if (prec == VA_PREC_AUTO) prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
+    // AUTO: bf16 when the pool holds at least 3k candidates. Without a caller's factor, fp32 rows
+    // take a 3k pool (wider than 128 from k = 43 on) to stay on bf16; otherwise (bf16 rows, a thin
+    // caller-set pool) the 4x smaller tf32 error keeps the true top k inside the pool. No pool
+    // size -> exact FP32 route.
+    if (prec == VA_PREC_AUTO) {
+        if (pool && pool < 3 * k && rerank == 0 && db->dtype == VA_DTYPE_F32 && 3 * k <= VA_MAX_SELECT_K)
+            pool = 3 * k;
+        prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
+    }
     if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
         if (!pool) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
         prec = VA_PREC_BF16;

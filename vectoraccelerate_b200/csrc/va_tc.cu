@@ -319,11 +319,16 @@ __device__ __forceinline__ float next_up(float v) {
     return nextafterf(v, INFINITY);
 }
 
-// Filter bound from the shared per-query key (0xFFFFFFFF = nothing published yet): the next
-// float above the published key, so keys equal to it still pass.
-__device__ __forceinline__ float load_bound(const uint32_t* g) {
-    const uint32_t k = __ldcg(g);
-    return k == 0xFFFFFFFFu ? INFINITY : next_up(va::key2f(k));
+// Filter bound from the shared per-query slots (0xFFFFFFFF = nothing published yet): the next
+// float above the largest slot's key, so keys equal to it still pass.
+__device__ __forceinline__ float load_bound(const uint32_t* g, int64_t stride, int nslots) {
+    uint32_t m = 0;
+    for (int s = 0; s < nslots; ++s) {
+        const uint32_t k = __ldcg(g + s * stride);
+        if (k == 0xFFFFFFFFu) return INFINITY;
+        m = k > m ? k : m;
+    }
+    return next_up(va::key2f(m));
 }
 
 struct Work {
@@ -339,9 +344,12 @@ struct Work {
     int cpr;
     int lag;
     uint32_t* sync_cnt;  // [rounds * cpr] arrivals per chunk slot, zeroed before the launch
-    // 1: items share a per-query bound (lists hold only what can reach the final KP pool);
-    // 0: every item's list is its exact top KP by (key, id), for pools wider than KP.
-    int share;
+    // Shared per-query bound in `nslots` slots ([nslots][nq_pad] keys): an item publishes its
+    // final KP-th key into slot (split % nslots) with atomicMin, and the bound is the largest slot
+    // (infinite while a slot is empty). The nslots slot minima are KP-th keys of nslots DISTINCT
+    // items, so at least nslots * KP candidates lie at or below the bound: with nslots =
+    // ceil(pool / KP) it never cuts into the final pool of `pool` candidates.
+    int nslots;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -513,7 +521,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = w.share ? load_bound(gthr + q) : INFINITY;
+            float thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
             float thr = thr_g;
             // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row): lane j
             // holds columns j + 32r, r < 8; the next tile's are prefetched while this one runs.
@@ -521,8 +529,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (w.share && ((t - t0) & 7) == 7) {
-                    thr_g = load_bound(gthr + q);
+                if (((t - t0) & 7) == 7) {
+                    thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
                     thr = fminf(thr_own, thr_g);
                 }
                 const int64_t col0 = (int64_t)t * BN;
@@ -567,10 +575,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             {
                 // Publish this item's KP-th key (finite once the list is full) as a bound.
-                if (w.share && thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
+                const int s = item / w.n_qtiles;
+                if (thr_own < INFINITY) atomicMin(gthr + (int64_t)(s % w.nslots) * w.nq_pad + q, va::f2key(thr_own));
                 // The warp's 32 lists are contiguous in shared memory and in the output
                 // ([split][query][KP]): copy them with coalesced stores.
-                const int s = item / w.n_qtiles;
                 const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
                     part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
@@ -839,14 +847,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = w.share ? load_bound(gthr + q) : INFINITY;
+            float thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
             float thr = thr_g;
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (w.share && ((t - t0) & 7) == 7) {
-                    thr_g = load_bound(gthr + q);
+                if (((t - t0) & 7) == 7) {
+                    thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
                     thr = fminf(thr_own, thr_g);
                 }
                 const int64_t col0 = (int64_t)t * BN;
@@ -887,8 +895,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
-                if (w.share && thr_own < INFINITY) atomicMin(gthr + q, va::f2key(thr_own));
                 const int s = item / w.n_qtiles;
+                if (thr_own < INFINITY) atomicMin(gthr + (int64_t)(s % w.nslots) * w.nq_pad + q, va::f2key(thr_own));
                 const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
                     part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
@@ -946,7 +954,7 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
                   const CUtensorMap& mx, const Work& w, int grid, bool pair) {
     auto kern = pair ? k_tc_filter_pair<ELEM, KP> : k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nq_pad * sizeof(uint32_t), ctx->stream));
+    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nslots * w.nq_pad * sizeof(uint32_t), ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
     // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
     // The pair kernel also runs as clusters of two CTAs.
@@ -1020,6 +1028,22 @@ int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan
     plan->cpr = (max_item_tiles + plan->chunk_tiles - 1) / plan->chunk_tiles;
     const int rounds = (plan->n_qtiles * splits + workers - 1) / workers;
     plan->sync_words = (int64_t)rounds * plan->cpr;
+    plan->bound_slots = 1;
+    return VA_OK;
+}
+
+// Plan for a final pool of `pool` candidates per query. Up to 128: one list of the pool's size
+// (32/64/128) per item and one bound slot. Wider: 64-entry lists (the single-CTA kernel) when the
+// row splits give at least twice the pool in list entries, else 128-entry lists, with
+// ceil(pool / kp) bound slots.
+int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPlan* plan) {
+    if (pool <= 128) {
+        VA_TRY(va_tc_plan(ctx, nq, n_rows, pool <= 32 ? 32 : pool <= 64 ? 64 : 128, plan));
+    } else {
+        VA_TRY(va_tc_plan(ctx, nq, n_rows, 64, plan));
+        if ((int64_t)plan->splits * 64 < 2 * (int64_t)pool) VA_TRY(va_tc_plan(ctx, nq, n_rows, 128, plan));
+    }
+    plan->bound_slots = (pool + plan->kp - 1) / plan->kp;
     return VA_OK;
 }
 
@@ -1045,7 +1069,7 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.cpr = p.cpr;
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
-    w.share = a.no_share ? 0 : 1;
+    w.nslots = a.bound_slots > 1 ? a.bound_slots : 1;
     if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
     const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);

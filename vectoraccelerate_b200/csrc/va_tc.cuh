@@ -18,6 +18,7 @@ struct TcPlan {
     int lag;             // chunks a CTA may run ahead of the slowest
     int cpr;             // chunk slots per round
     int64_t sync_words;  // size of the pacing counter array
+    int bound_slots;     // shared-bound slots per query (va_tc_plan sets 1; wider pools: ceil(pool/kp))
 };
 
 struct TcFilterArgs {
@@ -33,14 +34,17 @@ struct TcFilterArgs {
                             // then the exact integer row_bias - 2 * dot + row_qn (row_bias holds ints)
     float* part_keys;       // [splits][nq_pad][kp]
     uint32_t* part_ids;     // [splits][nq_pad][kp]
-    uint32_t* gthr;         // [nq_pad] shared per-query bound (orderable key), set to 0xFF bytes
+    uint32_t* gthr;         // [bound_slots][nq_pad] shared per-query bound slots (orderable keys),
+                            // set to 0xFF bytes by va_tc_filter
     uint32_t* sync_cnt;     // [sync_words] pacing counters, zeroed by va_tc_filter
     int64_t sync_words;
     unsigned limit_ms;    // bound of every device-side wait
-    int no_share;         // 1: no shared bound; each split's list is its exact top kp by (key, id)
+    int bound_slots;      // slots of the shared bound: ceil(pool / kp) for a final pool of `pool`
+                          // candidates (0 or 1: one slot, pool <= kp)
 };
 
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
+int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPlan* plan);
 int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
 int va_tc_stages(int kp, bool pair);
 bool va_tc_use_pair();

@@ -591,6 +591,19 @@ class BinaryDatabase(_DbHandle):
         self.handle = h.value
         self.id_base = id_base
 
+    @classmethod
+    def from_device(cls, context: GPUContext, codes_ptr: int, n: int, dim_bits: int, id_base: int = 0):
+        """A database copied from packed codes already in device memory ([n x ceil(dim_bits/32)])."""
+        self = cls.__new__(cls)
+        self.context = context
+        self.n, self.words, self.dim_bits = n, (dim_bits + 31) // 32, dim_bits
+        h = ctypes.c_void_p()
+        _ffi.call("va_db_create_binary", context.handle, codes_ptr, 1, n, dim_bits, id_base, ctypes.byref(h))
+        context.synchronize()
+        self.handle = h.value
+        self.id_base = id_base
+        return self
+
     def search(self, query_codes, k: int):
         """-> (distances uint32 [Q,k], ids uint32 [Q,k]), sorted by (distance, id)."""
         q = np.ascontiguousarray(query_codes, np.uint32)
