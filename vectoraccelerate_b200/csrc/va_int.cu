@@ -331,12 +331,6 @@ bool hscan_supported(int words, int64_t nq) {
     return nq <= HS_MAX_Q && (words == 4 || words == 8 || words == 16 || words == 32);
 }
 
-int pool_list_size(int want) {
-    if (want <= 32) return 32;
-    if (want <= 64) return 64;
-    if (want <= 128) return 128;
-    return 0;
-}
 
 // Filter over the database's integer codes for queries already encoded in q_codes / q_norms
 // (both [plan.nq_pad]); partial lists land in the returned workspace pointers.
@@ -370,6 +364,7 @@ int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntS
 int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s) {
     TcFilterArgs a = {};
     a.bound_slots = plan.bound_slots;
+    a.bound_rank = plan.bound_rank;
     a.q_op = s.q_codes;
     a.x_op = db->codes;
     a.elem_bytes = 1;
@@ -662,9 +657,8 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
                                                                  db->cpad, db->codes, db->code_norms);
         VA_TRY(va_check_launch("k_expand_bits"));
     }
-    const int kp = pool_list_size(k);
     TcPlan plan;
-    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, k, &plan));
     IntScratch s;
     VA_TRY(int_scratch(ctx, db, plan, &s));
     void* ws2;

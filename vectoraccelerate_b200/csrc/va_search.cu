@@ -407,6 +407,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
     a.bound_slots = plan.bound_slots;
+    a.bound_rank = plan.bound_rank;
     // Wide pools: failure list and the fallback's gathered queries and results, sized before any
     // kernel writes them.
     uint32_t* fail_cnt = nullptr;

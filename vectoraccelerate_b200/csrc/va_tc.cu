@@ -322,13 +322,20 @@ __device__ __forceinline__ float next_up(float v) {
 // Filter bound from the shared per-query slots (0xFFFFFFFF = nothing published yet): the next
 // float above the largest slot's key, so keys equal to it still pass.
 __device__ __forceinline__ float load_bound(const uint32_t* g, int64_t stride, int nslots) {
+    // Eight independent loads in flight per batch (the slots sit in L2).
     uint32_t m = 0;
-    for (int s = 0; s < nslots; ++s) {
-        const uint32_t k = __ldcg(g + s * stride);
-        if (k == 0xFFFFFFFFu) return INFINITY;
-        m = k > m ? k : m;
+    bool empty = false;
+    for (int s0 = 0; s0 < nslots; s0 += 8) {
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = s0 + j < nslots ? __ldcg(g + (s0 + j) * stride) : 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            empty |= v[j] == 0xFFFFFFFFu;
+            m = v[j] > m ? v[j] : m;
+        }
     }
-    return next_up(va::key2f(m));
+    return empty ? INFINITY : next_up(va::key2f(m));
 }
 
 struct Work {
@@ -344,12 +351,15 @@ struct Work {
     int cpr;
     int lag;
     uint32_t* sync_cnt;  // [rounds * cpr] arrivals per chunk slot, zeroed before the launch
-    // Shared per-query bound in `nslots` slots ([nslots][nq_pad] keys): an item publishes its
-    // final KP-th key into slot (split % nslots) with atomicMin, and the bound is the largest slot
-    // (infinite while a slot is empty). The nslots slot minima are KP-th keys of nslots DISTINCT
-    // items, so at least nslots * KP candidates lie at or below the bound: with nslots =
-    // ceil(pool / KP) it never cuts into the final pool of `pool` candidates.
+    // Shared per-query bound in `nslots` slots ([nslots][nq_pad] keys): while it runs (every 8
+    // tiles) and at its end, an item publishes the key at rank `rank` of its list (once the list
+    // holds that many) into slot (split % nslots) with atomicMin; the bound is the largest slot
+    // (infinite while a slot is empty). The slot minima come from nslots DISTINCT items, each
+    // holding `rank` real candidates at or below its published key, so at least nslots * rank
+    // candidates lie at or below the bound: with nslots * rank >= pool it never cuts into the
+    // final pool. A low rank over many slots gives a tight bound early.
     int nslots;
+    int rank;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -528,8 +538,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
+            uint32_t* const my_slot = gthr + (int64_t)((item / w.n_qtiles) % w.nslots) * w.nq_pad + q;
+            const float* const my_rank_key = l_key + (size_t)row * KP + (w.rank - 1);
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 7) == 7) {
+                    const float vr = *my_rank_key;
+                    if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
                     thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
                     thr = fminf(thr_own, thr_g);
                 }
@@ -574,9 +588,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
-                // Publish this item's KP-th key (finite once the list is full) as a bound.
+                // Publish this item's final rank key as a bound.
                 const int s = item / w.n_qtiles;
-                if (thr_own < INFINITY) atomicMin(gthr + (int64_t)(s % w.nslots) * w.nq_pad + q, va::f2key(thr_own));
+                const float vr = *my_rank_key;
+                if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
                 // The warp's 32 lists are contiguous in shared memory and in the output
                 // ([split][query][KP]): copy them with coalesced stores.
                 const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
@@ -852,8 +867,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
+            uint32_t* const my_slot = gthr + (int64_t)((item / w.n_qtiles) % w.nslots) * w.nq_pad + q;
+            const float* const my_rank_key = l_key + (size_t)row * KP + (w.rank - 1);
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 7) == 7) {
+                    const float vr = *my_rank_key;
+                    if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
                     thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
                     thr = fminf(thr_own, thr_g);
                 }
@@ -896,7 +915,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             {
                 const int s = item / w.n_qtiles;
-                if (thr_own < INFINITY) atomicMin(gthr + (int64_t)(s % w.nslots) * w.nq_pad + q, va::f2key(thr_own));
+                const float vr = *my_rank_key;
+                if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
                 const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
                     part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
@@ -1029,6 +1049,7 @@ int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan
     const int rounds = (plan->n_qtiles * splits + workers - 1) / workers;
     plan->sync_words = (int64_t)rounds * plan->cpr;
     plan->bound_slots = 1;
+    plan->bound_rank = kp;
     return VA_OK;
 }
 
@@ -1043,7 +1064,13 @@ int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPla
         VA_TRY(va_tc_plan(ctx, nq, n_rows, 64, plan));
         if ((int64_t)plan->splits * 64 < 2 * (int64_t)pool) VA_TRY(va_tc_plan(ctx, nq, n_rows, 128, plan));
     }
-    plan->bound_slots = (pool + plan->kp - 1) / plan->kp;
+    // Bound: the pool (at least the list length) must stay at or below it. About one slot per
+    // four splits, so each slot's minimum is taken over several items; rank = pool / slots.
+    const int target = std::max(pool, plan->kp);
+    int ns = std::max(1, std::min(plan->splits / 4, 8));
+    const int rank = std::min(plan->kp, (target + ns - 1) / ns);
+    plan->bound_rank = rank;
+    plan->bound_slots = (target + rank - 1) / rank;
     return VA_OK;
 }
 
@@ -1070,6 +1097,7 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
     w.nslots = a.bound_slots > 1 ? a.bound_slots : 1;
+    w.rank = a.bound_rank >= 1 && a.bound_rank <= p.kp ? a.bound_rank : p.kp;
     if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
     const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);

@@ -18,7 +18,8 @@ struct TcPlan {
     int lag;             // chunks a CTA may run ahead of the slowest
     int cpr;             // chunk slots per round
     int64_t sync_words;  // size of the pacing counter array
-    int bound_slots;     // shared-bound slots per query (va_tc_plan sets 1; wider pools: ceil(pool/kp))
+    int bound_slots;     // shared-bound slots per query (va_tc_plan: 1; va_tc_plan_pool: see there)
+    int bound_rank;      // list rank an item publishes into its slot (va_tc_plan: kp)
 };
 
 struct TcFilterArgs {
@@ -39,8 +40,9 @@ struct TcFilterArgs {
     uint32_t* sync_cnt;     // [sync_words] pacing counters, zeroed by va_tc_filter
     int64_t sync_words;
     unsigned limit_ms;    // bound of every device-side wait
-    int bound_slots;      // slots of the shared bound: ceil(pool / kp) for a final pool of `pool`
-                          // candidates (0 or 1: one slot, pool <= kp)
+    int bound_slots;      // slots of the shared bound (0 or 1: one); bound_slots * bound_rank must be
+                          // at least the final pool (the list length kp when the pool is the list)
+    int bound_rank;       // list rank each item publishes (0: kp)
 };
 
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
