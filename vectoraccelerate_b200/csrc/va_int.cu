@@ -363,8 +363,7 @@ int int_scratch(va_context* ctx, const va_database* db, const TcPlan& plan, IntS
 
 int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, const IntScratch& s) {
     TcFilterArgs a = {};
-    a.bound_slots = plan.bound_slots;
-    a.bound_rank = plan.bound_rank;
+    a.levels = plan.levels;
     a.q_op = s.q_codes;
     a.x_op = db->codes;
     a.elem_bytes = 1;

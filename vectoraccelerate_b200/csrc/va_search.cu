@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
                                                            const float* __restrict__ queries,
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
                                                            int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
-                                                           int nslots,
+                                                           BoundLevels lv,
                                                            float* __restrict__ out_vals,
                                                            uint32_t* __restrict__ out_ids,
                                                            uint32_t* __restrict__ fail_list,
@@ -141,13 +141,17 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         if (id == va::kInvalidId) return ~0ull;
         return va::composite(va::f2key(part_keys[off]), id);
     };
-    // The filter's shared bound (the largest of its nslots slots, each the smallest KP-th key
-    // published by the items of that slot) is at least the global pool_n-th key, so candidates
-    // above it cannot be in the pool: one pass keeps the rest in shared memory and the selection
-    // runs there. If more than MR_POOL survive, the selection runs over all candidates instead.
+    // The filter's shared bound (per level the largest slot, the smallest over levels) is at
+    // least the global pool_n-th key, so candidates above it cannot be in the pool: one pass
+    // keeps the rest in shared memory and the selection runs there. If more than MR_POOL
+    // survive, the selection runs over all candidates instead.
     const int64_t n_all = (int64_t)splits * kp;
-    uint32_t bound = gthr ? 0u : 0xFFFFFFFFu;
-    for (int sl = 0; gthr && sl < nslots; ++sl) bound = max(bound, gthr[(int64_t)sl * nq_pad + qi]);
+    uint32_t bound = 0xFFFFFFFFu;
+    for (int l = 0; gthr && l < lv.n; ++l) {
+        uint32_t m = 0;
+        for (int sl = 0; sl < lv.slots[l]; ++sl) m = max(m, gthr[(int64_t)(lv.off[l] + sl) * nq_pad + qi]);
+        bound = min(bound, m);
+    }
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < n_all; i += blockDim.x) {
@@ -406,8 +410,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     a.sync_words = plan.sync_words;
     // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
     a.limit_ms = 2000u;
-    a.bound_slots = plan.bound_slots;
-    a.bound_rank = plan.bound_rank;
+    a.levels = plan.levels;
     // Wide pools: failure list and the fallback's gathered queries and results, sized before any
     // kernel writes them.
     uint32_t* fail_cnt = nullptr;
@@ -450,8 +453,8 @@ int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
                                                                     plan.kp, pool_n > 0 ? pool_n : plan.kp, queries,
                                                                     db->rows, db->dtype, db->dim,
-                                                                    metric, k, db->id_base, gthr,
-                                                                    std::max(1, plan.bound_slots), out_vals, out_ids,
+                                                                    metric, k, db->id_base, gthr, plan.levels,
+                                                                    out_vals, out_ids,
                                                                     fail_list, fail_cnt);
     return va_check_launch("k_merge_rerank");
 }

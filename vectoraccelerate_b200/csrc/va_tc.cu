@@ -319,23 +319,39 @@ __device__ __forceinline__ float next_up(float v) {
     return nextafterf(v, INFINITY);
 }
 
-// Filter bound from the shared per-query slots (0xFFFFFFFF = nothing published yet): the next
-// float above the largest slot's key, so keys equal to it still pass.
-__device__ __forceinline__ float load_bound(const uint32_t* g, int64_t stride, int nslots) {
-    // Eight independent loads in flight per batch (the slots sit in L2).
-    uint32_t m = 0;
-    bool empty = false;
-    for (int s0 = 0; s0 < nslots; s0 += 8) {
-        uint32_t v[8];
+// Filter bound from the shared per-query slots (0xFFFFFFFF = nothing published yet): per level
+// the largest slot (infinite while one is empty), the smallest over levels, then the next float
+// above it so keys equal to it still pass. g points at this query's column of slot 0.
+__device__ __forceinline__ float load_bound(const uint32_t* g, int64_t stride, const BoundLevels& lv) {
+    float best = INFINITY;
+    for (int l = 0; l < lv.n; ++l) {
+        const uint32_t* gl = g + (int64_t)lv.off[l] * stride;
+        const int ns = lv.slots[l];
+        uint32_t m = 0;
+        bool empty = false;
+        // Eight independent loads in flight per batch (the slots sit in L2).
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            uint32_t v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = s0 + j < nslots ? __ldcg(g + (s0 + j) * stride) : 0u;
+            for (int j = 0; j < 8; ++j) v[j] = s0 + j < ns ? __ldcg(gl + (s0 + j) * stride) : 0u;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            empty |= v[j] == 0xFFFFFFFFu;
-            m = v[j] > m ? v[j] : m;
+            for (int j = 0; j < 8; ++j) {
+                empty |= v[j] == 0xFFFFFFFFu;
+                m = v[j] > m ? v[j] : m;
+            }
         }
+        if (!empty) best = fminf(best, next_up(va::key2f(m)));
     }
-    return empty ? INFINITY : next_up(va::key2f(m));
+    return best;
+}
+
+// Publish a list's keys at each level's rank into the item's slot of that level.
+__device__ __forceinline__ void publish_bound(uint32_t* g, int64_t stride, const BoundLevels& lv, int split,
+                                              const float* row_keys) {
+    for (int l = 0; l < lv.n; ++l) {
+        const float v = row_keys[lv.rank[l] - 1];
+        if (v < INFINITY) atomicMin(g + (int64_t)(lv.off[l] + split % lv.slots[l]) * stride, va::f2key(v));
+    }
 }
 
 struct Work {
@@ -351,15 +367,16 @@ struct Work {
     int cpr;
     int lag;
     uint32_t* sync_cnt;  // [rounds * cpr] arrivals per chunk slot, zeroed before the launch
-    // Shared per-query bound in `nslots` slots ([nslots][nq_pad] keys): while it runs (every 8
-    // tiles) and at its end, an item publishes the key at rank `rank` of its list (once the list
-    // holds that many) into slot (split % nslots) with atomicMin; the bound is the largest slot
-    // (infinite while a slot is empty). The slot minima come from nslots DISTINCT items, each
-    // holding `rank` real candidates at or below its published key, so at least nslots * rank
-    // candidates lie at or below the bound: with nslots * rank >= pool it never cuts into the
-    // final pool. A low rank over many slots gives a tight bound early.
-    int nslots;
-    int rank;
+    // Shared per-query bound ([total slots][nq_pad] keys) in levels: while it runs (every 4
+    // tiles) and at its end, an item publishes, for each level, the key at the level's list rank
+    // (once the list holds that many) into slot (split % slots) of the level with atomicMin. A
+    // level's bound is its largest slot (infinite while a slot is empty): the slot minima come
+    // from `slots` DISTINCT items, each holding `rank` real candidates at or below its key, so
+    // at least slots * rank candidates lie at or below it, and with slots * rank >= the final
+    // pool it never cuts into the pool. Every level is valid, so the filter uses the smallest.
+    // One slot at a high rank is available after the first item's first tiles; many slots at a
+    // low rank are tighter once items of every split class have run.
+    BoundLevels lv;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -378,6 +395,15 @@ __device__ __forceinline__ bool wait_arrivals(const uint32_t* p, uint32_t target
         if (va::globaltimer_ns() - t0 > limit_ns) return false;
     }
     return true;
+}
+
+BoundLevels one_level(int kp) {
+    BoundLevels lv = {};
+    lv.n = 1;
+    lv.slots[0] = 1;
+    lv.rank[0] = kp;
+    lv.off[0] = 0;
+    return lv;
 }
 
 __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int& t0, int& t1) {
@@ -531,20 +557,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
+            float thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
             float thr = thr_g;
             // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row): lane j
             // holds columns j + 32r, r < 8; the next tile's are prefetched while this one runs.
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
-            uint32_t* const my_slot = gthr + (int64_t)((item / w.n_qtiles) % w.nslots) * w.nq_pad + q;
-            const float* const my_rank_key = l_key + (size_t)row * KP + (w.rank - 1);
+            const int split = item / w.n_qtiles;
+            const float* const row_keys = l_key + (size_t)row * KP;
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (((t - t0) & 7) == 7) {
-                    const float vr = *my_rank_key;
-                    if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
-                    thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
+                if (((t - t0) & 3) == 3) {
+                    publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
+                    thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
                     thr = fminf(thr_own, thr_g);
                 }
                 const int64_t col0 = (int64_t)t * BN;
@@ -588,10 +613,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
-                // Publish this item's final rank key as a bound.
-                const int s = item / w.n_qtiles;
-                const float vr = *my_rank_key;
-                if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
+                // Publish this item's final rank keys as bounds.
+                const int s = split;
+                publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
                 // The warp's 32 lists are contiguous in shared memory and in the output
                 // ([split][query][KP]): copy them with coalesced stores.
                 const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
@@ -862,18 +886,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qn = row_qn ? row_qn[q] : 0;
             const uint32_t n_rows32 = (uint32_t)w.n_rows;
             float thr_own = INFINITY;
-            float thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
+            float thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
             float thr = thr_g;
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
-            uint32_t* const my_slot = gthr + (int64_t)((item / w.n_qtiles) % w.nslots) * w.nq_pad + q;
-            const float* const my_rank_key = l_key + (size_t)row * KP + (w.rank - 1);
+            const int split = item / w.n_qtiles;
+            const float* const row_keys = l_key + (size_t)row * KP;
             for (int t = t0; t < t1; ++t, ++tile) {
-                if (((t - t0) & 7) == 7) {
-                    const float vr = *my_rank_key;
-                    if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
-                    thr_g = load_bound(gthr + q, w.nq_pad, w.nslots);
+                if (((t - t0) & 3) == 3) {
+                    publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
+                    thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
                     thr = fminf(thr_own, thr_g);
                 }
                 const int64_t col0 = (int64_t)t * BN;
@@ -914,9 +937,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int r = 0; r < 8; ++r) bias[r] = nbias[r];
             }
             {
-                const int s = item / w.n_qtiles;
-                const float vr = *my_rank_key;
-                if (vr < INFINITY) atomicMin(my_slot, va::f2key(vr));
+                const int s = split;
+                publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
                 const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
                     part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
@@ -974,7 +996,9 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
                   const CUtensorMap& mx, const Work& w, int grid, bool pair) {
     auto kern = pair ? k_tc_filter_pair<ELEM, KP> : k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)w.nslots * w.nq_pad * sizeof(uint32_t), ctx->stream));
+    int total_slots = 0;
+    for (int l = 0; l < w.lv.n; ++l) total_slots += w.lv.slots[l];
+    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)total_slots * w.nq_pad * sizeof(uint32_t), ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
     // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
     // The pair kernel also runs as clusters of two CTAs.
@@ -1048,8 +1072,8 @@ int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan
     plan->cpr = (max_item_tiles + plan->chunk_tiles - 1) / plan->chunk_tiles;
     const int rounds = (plan->n_qtiles * splits + workers - 1) / workers;
     plan->sync_words = (int64_t)rounds * plan->cpr;
+    plan->levels = one_level(kp);
     plan->bound_slots = 1;
-    plan->bound_rank = kp;
     return VA_OK;
 }
 
@@ -1064,13 +1088,28 @@ int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPla
         VA_TRY(va_tc_plan(ctx, nq, n_rows, 64, plan));
         if ((int64_t)plan->splits * 64 < 2 * (int64_t)pool) VA_TRY(va_tc_plan(ctx, nq, n_rows, 128, plan));
     }
-    // Bound: the pool (at least the list length) must stay at or below it. About one slot per
-    // four splits, so each slot's minimum is taken over several items; rank = pool / slots.
+    // Bound levels: the pool (at least the list length) must stay at or below each. Ranks kp,
+    // kp/2, kp/4, kp/8 with slots = ceil(target / rank), while the slots have items to feed them
+    // (slots <= splits) and the total stays within 32 loads per refresh.
     const int target = std::max(pool, plan->kp);
-    int ns = std::max(1, std::min(plan->splits / 4, 8));
-    const int rank = std::min(plan->kp, (target + ns - 1) / ns);
-    plan->bound_rank = rank;
-    plan->bound_slots = (target + rank - 1) / rank;
+    BoundLevels lv = {};
+    int total = 0;
+    for (int r = plan->kp; r >= 1 && lv.n < 4 && r * 8 >= plan->kp; r /= 2) {
+        const int ns = (target + r - 1) / r;
+        if (ns > plan->splits || total + ns > 32) break;
+        lv.slots[lv.n] = ns;
+        lv.rank[lv.n] = r;
+        lv.off[lv.n] = total;
+        total += ns;
+        ++lv.n;
+    }
+    if (!lv.n) {
+        lv = one_level(plan->kp);
+        lv.slots[0] = (target + plan->kp - 1) / plan->kp;
+        total = lv.slots[0];
+    }
+    plan->levels = lv;
+    plan->bound_slots = total;
     return VA_OK;
 }
 
@@ -1096,8 +1135,11 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.cpr = p.cpr;
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
-    w.nslots = a.bound_slots > 1 ? a.bound_slots : 1;
-    w.rank = a.bound_rank >= 1 && a.bound_rank <= p.kp ? a.bound_rank : p.kp;
+    w.lv = a.levels.n > 0 ? a.levels : one_level(p.kp);
+    for (int l = 0; l < w.lv.n; ++l)
+        if (w.lv.rank[l] < 1 || w.lv.rank[l] > p.kp || w.lv.slots[l] < 1)
+            return va_set_error(VA_ERR_INVALID_ARG, "bound level %d: rank %d / slots %d invalid for lists of %d", l,
+                                w.lv.rank[l], w.lv.slots[l], p.kp);
     if (a.sync_words < p.sync_words) return va_set_error(VA_ERR_INVALID_ARG, "sync buffer too small");
     const int stages = va_tc_stages(p.kp, p.pair);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d too large for shared memory", p.kp);

@@ -6,6 +6,16 @@ struct va_context;
 
 // Work decomposition of one filter launch: (query tile of 128) x (row split) items, statically
 // strided over a persistent grid of at most one CTA per SM.
+// Levels of the shared per-query bound (see the filter kernel): level l has `slots[l]` slots
+// starting at slot `off[l]`, fed with the key at list rank `rank[l]`; slots[l] * rank[l] is at
+// least the final pool. n = 0 means one level of one slot at rank kp.
+struct BoundLevels {
+    int n;
+    int slots[4];
+    int rank[4];
+    int off[4];
+};
+
 struct TcPlan {
     int n_qtiles;
     int n_tiles;
@@ -18,8 +28,8 @@ struct TcPlan {
     int lag;             // chunks a CTA may run ahead of the slowest
     int cpr;             // chunk slots per round
     int64_t sync_words;  // size of the pacing counter array
-    int bound_slots;     // shared-bound slots per query (va_tc_plan: 1; va_tc_plan_pool: see there)
-    int bound_rank;      // list rank an item publishes into its slot (va_tc_plan: kp)
+    int bound_slots;     // shared-bound slots per query, all levels (the gthr array's height)
+    BoundLevels levels;  // va_tc_plan: one slot at rank kp; va_tc_plan_pool: up to four levels
 };
 
 struct TcFilterArgs {
@@ -35,14 +45,13 @@ struct TcFilterArgs {
                             // then the exact integer row_bias - 2 * dot + row_qn (row_bias holds ints)
     float* part_keys;       // [splits][nq_pad][kp]
     uint32_t* part_ids;     // [splits][nq_pad][kp]
-    uint32_t* gthr;         // [bound_slots][nq_pad] shared per-query bound slots (orderable keys),
+    uint32_t* gthr;         // [total slots][nq_pad] shared per-query bound slots (orderable keys),
                             // set to 0xFF bytes by va_tc_filter
     uint32_t* sync_cnt;     // [sync_words] pacing counters, zeroed by va_tc_filter
     int64_t sync_words;
     unsigned limit_ms;    // bound of every device-side wait
-    int bound_slots;      // slots of the shared bound (0 or 1: one); bound_slots * bound_rank must be
-                          // at least the final pool (the list length kp when the pool is the list)
-    int bound_rank;       // list rank each item publishes (0: kp)
+    BoundLevels levels;   // bound levels (levels.n = 0: one slot at rank kp); every level's
+                          // slots * rank must be at least the final pool (kp when the pool is the list)
 };
 
 int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
