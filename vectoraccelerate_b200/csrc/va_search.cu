@@ -154,11 +154,16 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
     }
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < n_all; i += blockDim.x) {
-        const uint64_t c = get(i);
-        if (c != ~0ull && (uint32_t)(c >> 32) <= bound) {
+    // Lists are sorted by key: one thread walks each split's list and stops at the first key
+    // above the bound or the first empty entry, so only the useful prefix is read.
+    for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+        const int64_t off = ((int64_t)s * nq_pad + qi) * kp;
+        for (int j = 0; j < kp; ++j) {
+            const uint32_t key = va::f2key(part_keys[off + j]);
+            const uint32_t id = part_ids[off + j];
+            if (key > bound || id == va::kInvalidId) break;
             const int slot = atomicAdd(&s_cnt, 1);
-            if (slot < MR_POOL) pool[slot] = c;
+            if (slot < MR_POOL) pool[slot] = va::composite(key, id);
         }
     }
     __syncthreads();
@@ -210,7 +215,33 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         }
         const int64_t base = (int64_t)id * dim;
         double s = 0, xx = 0;
-        if (metric == VA_METRIC_L2SQ) {
+        if ((dim & 127) == 0) {
+            // 16-byte (fp32) or 8-byte (bf16) loads of four consecutive elements per lane: the
+            // row's loads are independent and in flight together.
+#pragma unroll 4
+            for (int j0 = lane * 4; j0 < dim; j0 += 128) {
+                const float4 qv = *(const float4*)(sq + j0);
+                float4 xv;
+                if (dtype == VA_DTYPE_BF16) {
+                    const uint2 u = __ldg((const uint2*)((const uint16_t*)rows + base + j0));
+                    xv = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+                } else {
+                    xv = __ldg((const float4*)((const float*)rows + base + j0));
+                }
+                const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (metric == VA_METRIC_L2SQ) {
+                        const double t = (double)qa[e] - (double)xa[e];
+                        s += t * t;
+                    } else {
+                        s += (double)qa[e] * (double)xa[e];
+                        xx += (double)xa[e] * (double)xa[e];
+                    }
+                }
+            }
+        } else if (metric == VA_METRIC_L2SQ) {
             for (int j = lane; j < dim; j += 32) {
                 double t = (double)sq[j] - (double)load_row(rows, dtype, base + j);
                 s += t * t;
@@ -221,8 +252,8 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
                 s += (double)sq[j] * xv;
                 xx += xv * xv;
             }
-            if (metric == VA_METRIC_COSINE) xx = warp_sum_d(xx);
         }
+        if (metric == VA_METRIC_COSINE) xx = warp_sum_d(xx);
         s = warp_sum_d(s);
         if (lane == 0) {
             float v;
