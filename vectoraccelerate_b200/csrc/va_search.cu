@@ -647,11 +647,14 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     // AUTO: bf16 when the pool holds at least 3k candidates. Without a caller's factor, fp32 rows
     // take a 3k pool (wider than 128 from k = 43 on) to stay on bf16; otherwise (bf16 rows, a thin
     // caller-set pool) the 4x smaller tf32 error keeps the true top k inside the pool. No pool
-    // size -> exact FP32 route.
+    // size -> exact FP32 route. Rows of at most 16 dimensions (fp32) take the FP32 route too: few
+    // dimensions give the reduced-precision keys no resolution between close neighbours (for
+    // d = 1 a bf16 key cannot order points 1/N apart), and the SIMT route is cheap there.
     if (prec == VA_PREC_AUTO) {
         if (pool && pool < 3 * k && rerank == 0 && db->dtype == VA_DTYPE_F32 && 3 * k <= VA_MAX_SELECT_K)
             pool = 3 * k;
         prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
+        if (db->dim <= 16 && db->dtype == VA_DTYPE_F32) prec = VA_PREC_FP32;
     }
     if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
         if (!pool) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
