@@ -414,11 +414,6 @@ def run_config(a):
     ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
     n_total = a.n
     note = None
-    if kind == "binary" and world == 1 and a.nq > 8 and n_total > 100_000_000:
-        # the tensor-core route holds the 0/1 expansion (1 KB per 1024-bit row): 200M rows need
-        # two GPUs; one GPU takes half the database
-        n_total = 100_000_000
-        note = "1 GPU: N = 100M (the 0/1 expansion of 200M codes exceeds one GPU's HBM); N = 200M from 2 GPUs"
     row0, n_local = shard_bounds(n_total, world, rank)
     dim, nq, k = a.dim, a.nq, a.k
     chunk = max(1, (4 << 30) // (4 * dim))  # fp32 generation chunks of <= 4 GiB

@@ -57,7 +57,8 @@ extern "C" {
 
 /* Contraction precision of the fused search. Reduced-precision passes are always followed by an
  * exact rerank of the candidates, so results equal the exact search's apart from stated ties. */
-#define VA_PREC_AUTO 0 /* BF16 tensor cores when the row layout allows, else FP32            */
+#define VA_PREC_AUTO 0 /* BF16 with a pool of >= 3k candidates (TF32 for bf16 rows at large k,
+                          FP32 when no pool fits or d <= 16)                                  */
 #define VA_PREC_FP32 1 /* exact fp32 SIMT contraction, chunked, no rerank needed             */
 #define VA_PREC_TF32 2 /* tcgen05 kind::tf32 on the fp32 rows + exact rerank                 */
 #define VA_PREC_BF16 3 /* tcgen05 kind::f16 (bf16) + exact rerank                            */
@@ -277,6 +278,11 @@ int va_hamming_knn(va_context* ctx, const uint32_t* q, int64_t nq, const uint32_
  * Metal4BinaryVector, BinaryQuantizationKernel.swift:23-74), host or device. */
 int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
                         uint32_t id_base, va_database** out);
+/* Rows expanded per pass of the batched search (rounded down to a multiple of 256; 0 =
+ * automatic: the whole 0/1 expansion (dim_bits bytes per row) is kept resident when it fits in 60%
+ * of the free device memory, otherwise chunks of half the free memory are expanded per pass).
+ * Must be called before the first batched search. No counterpart in the reference. */
+int va_db_binary_set_chunk_rows(va_database* db, int64_t rows);
 /* Batched Hamming k-NN over a binary database on the integer tensor cores: popcount(q ^ x) =
  * |q| + |x| - 2 q.x over the 0/1 bits, exact; results sorted by (distance, id), k <= 128. Same
  * results as va_hamming_knn (HammingDistanceKernel.computeBitPacked + nearestNeighbors,

@@ -171,3 +171,23 @@ def test_hamming_db_small_batch_ties(ctx, oracle):
         db.close()
     assert np.array_equal(gd, od) and np.array_equal(gi, oi)
     assert np.array_equal(gd1, od[:1]) and np.array_equal(gi1, oi[:1])
+
+
+@pytest.mark.parametrize("chunk", [5000, 256])
+def test_hamming_db_chunked_expansion(ctx, oracle, chunk):
+    """Batches over a database expanded chunk by chunk (the route of databases whose 0/1
+    expansion does not fit): same results, ties across chunk boundaries included."""
+    import vectoraccelerate_b200 as va
+    base = oracle.binary_quantize(oracle.gen_gaussian(3000, 512, 12))
+    x = np.concatenate([base, base[:2000]])  # duplicates in different chunks
+    q = oracle.binary_quantize(oracle.gen_gaussian(150, 512, 13, row0=QROW))
+    q[:5] = base[[0, 100, 1999, 2500, 2999]]
+    oi, od = oracle.hamming_knn(q, x, 64)
+    db = va.BinaryDatabase(ctx, x, 512, id_base=3)
+    try:
+        db.set_chunk_rows(chunk)
+        gd, gi = db.search(q, 64)
+    finally:
+        db.close()
+    assert np.array_equal(gd, od)
+    assert np.array_equal(gi - np.uint32(3), oi)

@@ -83,6 +83,7 @@ SIGNATURES = {
     "va_hamming_matrix": [_P, _P, _I64, _P, _I64, _I, _P, _P, _I],
     "va_hamming_knn": [_P, _P, _I64, _P, _I64, _I, _I, _P, _P],
     "va_db_create_binary": [_P, _P, _I, _I64, _I, _U32, _PP],
+    "va_db_binary_set_chunk_rows": [_P, _I64],
     "va_hamming_knn_db": [_P, _P, _P, _I64, _I, _P, _P],
     "va_gen_gaussian": [_P, _P, _I64, _I, _U64, _I64],
     "va_gen_mixture": [_P, _P, _I64, _I, _U64, _I64, _I, _F, _I],

@@ -444,6 +444,67 @@ int alloc_int_db(va_context* ctx, va_database* db, int64_t n, int cpad) {
 
 }  // namespace
 
+namespace {
+
+// Filter + list merge of nq expanded queries over one database view; results [nq x k] as distance
+// bit patterns and view-local ids.
+int hamming_view(va_context* ctx, const va_database* view, const uint32_t* queries, int64_t nq, int k, float* out_v,
+                 uint32_t* out_i) {
+    TcPlan plan;
+    VA_TRY(va_tc_plan_pool(ctx, nq, view->n, k, &plan));
+    IntScratch s;
+    VA_TRY(int_scratch(ctx, view, plan, &s));
+    k_expand_bits<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, view->words, view->cpad,
+                                                                    s.q_codes, s.q_norms);
+    VA_TRY(va_check_launch("k_expand_bits(queries)"));
+    VA_TRY(run_int_filter(ctx, view, plan, s));
+    return va_merge_lists_internal(ctx, s.part_keys, s.part_ids, plan.splits, plan.nq_pad * plan.kp, plan.kp, nq, k,
+                                   VA_SELECT_MIN, out_v, out_i);
+}
+
+// Chunked route: expand rows [r0, r0 + stage_rows) into the staging buffer, search them, keep
+// each chunk's k best (global ids), merge the chunks' lists.
+int hamming_chunked(va_context* ctx, va_database* db, const uint32_t* queries, int64_t nq, int k, uint32_t* out_dists,
+                    uint32_t* out_ids) {
+    const int64_t n = db->n, cr = db->stage_rows;
+    const int64_t nch = (n + cr - 1) / cr;
+    const size_t lb = (size_t)nch * nq * k;
+    void* aux;
+    VA_TRY(va_aux_buffer(ctx, lb * 8 + (size_t)nq * k * 4 + 512, &aux));
+    float* cv = (float*)aux;
+    uint32_t* ci = (uint32_t*)(cv + lb);
+    float* mv = (float*)(ci + lb);
+    const int blocks = std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096));
+    const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+    for (int64_t c = 0; c < nch; ++c) {
+        const int64_t r0 = c * cr, rows = std::min(cr, n - r0);
+        k_expand_bits<<<warps_grid(rows), 256, 0, ctx->stream>>>((const uint32_t*)db->rows + r0 * db->words, rows,
+                                                                rows, db->words, db->cpad, db->stage, db->stage_norms);
+        VA_TRY(va_check_launch("k_expand_bits(chunk)"));
+        va_database view = *db;
+        view.codes = db->stage;
+        view.code_norms = db->stage_norms;
+        view.n = rows;
+        view.id_base = 0;
+        float* v = cv + (size_t)c * nq * k;
+        uint32_t* ids = ci + (size_t)c * nq * k;
+        VA_TRY(hamming_view(ctx, &view, queries, nq, k, v, ids));
+        if (r0) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(ids, nq * k, (uint32_t)r0);
+    }
+    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+    if (prof)
+        ctx->prof_n++;
+    else
+        ctx->k_recorded = true;
+    VA_TRY(va_merge_lists_internal(ctx, cv, ci, (int)nch, nq * k, k, nq, k, VA_SELECT_MIN, mv, out_ids));
+    if (out_dists) k_bits_to_dists<<<blocks, 256, 0, ctx->stream>>>(mv, out_ids, nq * k, out_dists);
+    if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
+    return va_check_launch("k_bits_to_dists");
+}
+
+}  // namespace
+
 extern "C" {
 
 int va_sq_perdim_minmax(va_context* ctx, const float* x, int64_t n, int dim, float* out_min, float* out_max) {
@@ -603,6 +664,15 @@ int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, i
     return VA_OK;
 }
 
+int va_db_binary_set_chunk_rows(va_database* db, int64_t rows) {
+    VA_REQUIRE(db, "db must not be NULL");
+    VA_REQUIRE(db->kind == VA_DB_BINARY, "database is not a binary database");
+    VA_REQUIRE(rows >= 0, "rows must be >= 0, got %lld", (long long)rows);
+    VA_REQUIRE(!db->codes && !db->stage, "the expansion of this database is already built");
+    db->chunk_request = rows ? std::max<int64_t>(256, rows / 256 * 256) : 0;
+    return VA_OK;
+}
+
 int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* queries, int64_t nq, int k,
                       uint32_t* out_dists, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && queries && out_ids, "ctx, db, queries and out_ids must not be NULL");
@@ -649,13 +719,36 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
         if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
         return va_check_launch("k_bits_to_dists");
     }
-    // Batches: the 0/1 expansion of the codes (built on first use) on the integer tensor cores.
-    if (!db->codes) {
-        VA_TRY(alloc_int_db(ctx, db, db->n, db->cpad));
-        k_expand_bits<<<warps_grid(db->n), 256, 0, ctx->stream>>>((const uint32_t*)db->rows, db->n, db->n, db->words,
-                                                                 db->cpad, db->codes, db->code_norms);
-        VA_TRY(va_check_launch("k_expand_bits"));
+    // Batches: the 0/1 expansion of the codes on the integer tensor cores. It is built once, on
+    // first use, when it fits in 60% of the free device memory; otherwise (or when the caller set
+    // a chunk size) chunks of rows are expanded and searched one at a time.
+    if (!db->codes && !db->stage) {
+        size_t free_b = 0, total_b = 0;
+        VA_CUDA_TRY(cudaMemGetInfo(&free_b, &total_b));
+        const double need = (double)db->n * db->cpad + (double)round_up(db->n, 256) * 4;
+        if (!db->chunk_request && need <= 0.6 * (double)free_b) {
+            VA_TRY(alloc_int_db(ctx, db, db->n, db->cpad));
+            k_expand_bits<<<warps_grid(db->n), 256, 0, ctx->stream>>>((const uint32_t*)db->rows, db->n, db->n,
+                                                                     db->words, db->cpad, db->codes, db->code_norms);
+            VA_TRY(va_check_launch("k_expand_bits"));
+        } else {
+            int64_t rows = db->chunk_request ? db->chunk_request
+                                             : (int64_t)(0.5 * (double)free_b / (double)(db->cpad + 4)) / 256 * 256;
+            rows = std::min<int64_t>(std::max<int64_t>(rows, 256), db->n);
+            cudaError_t e = cudaMalloc((void**)&db->stage, (size_t)rows * db->cpad);
+            if (e == cudaSuccess) e = cudaMalloc((void**)&db->stage_norms, (size_t)round_up(rows, 256) * 4);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                if (db->stage) cudaFree(db->stage);
+                db->stage = nullptr;
+                return va_set_error(VA_ERR_OOM, "staging for %lld expanded rows failed: %s", (long long)rows,
+                                    cudaGetErrorString(e));
+            }
+            VA_CUDA_TRY(cudaMemsetAsync(db->stage_norms, 0, (size_t)round_up(rows, 256) * 4, ctx->stream));
+            db->stage_rows = rows;
+        }
     }
+    if (!db->codes) return hamming_chunked(ctx, db, queries, nq, k, out_dists, out_ids);
     TcPlan plan;
     VA_TRY(va_tc_plan_pool(ctx, nq, db->n, k, &plan));
     IntScratch s;

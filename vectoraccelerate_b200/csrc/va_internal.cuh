@@ -98,6 +98,11 @@ struct va_database {
     float* sq_scales = nullptr;  // int8: per-dimension scale
     int cpad = 0;                // code row length (multiple of 128)
     int words = 0;               // binary: 32-bit words per code
+    // Binary databases whose 0/1 expansion does not fit: one chunk of rows is expanded at a time.
+    int8_t* stage = nullptr;     // [stage_rows x cpad] 0/1 bytes of the current chunk
+    int* stage_norms = nullptr;  // popcounts of the current chunk (padded to 256 rows)
+    int64_t stage_rows = 0;      // rows per chunk (0: not chunked)
+    int64_t chunk_request = 0;   // rows per chunk set by the caller (0: automatic)
 };
 
 #define VA_DB_FLOAT 0

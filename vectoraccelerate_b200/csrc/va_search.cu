@@ -595,6 +595,8 @@ int va_db_destroy(va_database* db) {
     cudaSetDevice(db->ctx->device);
     cudaStreamSynchronize(db->ctx->stream);
     if (db->op && !db->op_alias) cudaFree(db->op);
+    if (db->stage) cudaFree(db->stage);
+    if (db->stage_norms) cudaFree(db->stage_norms);
     if (db->op_cos) cudaFree(db->op_cos);
     if (db->op_f32 && !db->op_f32_alias) cudaFree(db->op_f32);
     if (db->op_f32_cos) cudaFree(db->op_f32_cos);

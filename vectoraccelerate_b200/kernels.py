@@ -604,6 +604,10 @@ class BinaryDatabase(_DbHandle):
         self.id_base = id_base
         return self
 
+    def set_chunk_rows(self, rows: int):
+        """Rows expanded per pass of batched searches (0: automatic); before the first search."""
+        _ffi.call("va_db_binary_set_chunk_rows", self.handle, rows)
+
     def search(self, query_codes, k: int):
         """-> (distances uint32 [Q,k], ids uint32 [Q,k]), sorted by (distance, id)."""
         q = np.ascontiguousarray(query_codes, np.uint32)
