@@ -112,18 +112,34 @@ __global__ void k_perdim_codes(const float* __restrict__ x, int64_t n_valid, int
     if (lane == 0 && norms) norms[r] = acc;
 }
 
-// 0/1 bytes of LSB-first packed codes [n_out x cpad] and popcounts. One warp per row.
+// Four bits (LSB first) -> four 0/1 bytes of a little-endian word.
+__device__ __forceinline__ uint32_t spread4(uint32_t x) {
+    return (x & 1u) | ((x & 2u) << 7) | ((x & 4u) << 14) | ((x & 8u) << 21);
+}
+
+// 0/1 bytes of LSB-first packed codes [n_out x cpad] and popcounts. One warp per row; each lane
+// expands whole 32-bit words into 32 bytes (two 16-byte stores).
 __global__ void k_expand_bits(const uint32_t* __restrict__ codes, int64_t n_valid, int64_t n_out, int words, int cpad,
                               int8_t* __restrict__ out, int* __restrict__ pops) {
     const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (r >= n_out) return;
     int acc = 0;
-    for (int j = lane; j < cpad; j += 32) {
-        int b = 0;
-        if (r < n_valid && j < words * 32) b = (int)((codes[r * words + (j >> 5)] >> (j & 31)) & 1u);
-        out[r * cpad + j] = (int8_t)b;
-        acc += b;
+    for (int w = lane; w < cpad / 32; w += 32) {
+        const uint32_t x = (r < n_valid && w < words) ? __ldg(codes + r * words + w) : 0u;
+        acc += __popc(x);
+        uint4 lo, hi;
+        lo.x = spread4(x);
+        lo.y = spread4(x >> 4);
+        lo.z = spread4(x >> 8);
+        lo.w = spread4(x >> 12);
+        hi.x = spread4(x >> 16);
+        hi.y = spread4(x >> 20);
+        hi.z = spread4(x >> 24);
+        hi.w = spread4(x >> 28);
+        uint4* o = (uint4*)(out + r * cpad + (int64_t)w * 32);
+        o[0] = lo;
+        o[1] = hi;
     }
     acc = warp_sum_i(acc);
     if (lane == 0) pops[r] = acc;
