@@ -12,6 +12,7 @@ from .context import DeviceBuffer, GPUContext, Metal4Configuration, Metal4Contex
 from .errors import (BufferAllocationFailed, CollectiveFailed, ComputeFailed, InvalidInput, Timeout, Unsupported,
                      VectorError)
 from .index import AcceleratedVectorIndex, IndexConfiguration, IndexSearchResult, SearchResults, VectorHandle
+from .provider import MetalComputeProvider
 from .kernels import (BinaryDatabase, BinaryQuantizationKernel, CosineSimilarityKernel, Database, DotProductKernel,
                       FusedL2TopKKernel, Int8Database, FusedL2TopKParameters, HammingDistanceKernel, L2DistanceKernel,
                       Metal4BinaryVector, Metal4FusedL2Config, Metal4FusedL2TopKResult, Metal4QuantizationResult,
