@@ -183,6 +183,17 @@ int va_db_info(const va_database* db, int64_t* n, int* dim, int* dtype);
 /* Device pointer of the database's original rows (fp32 or bf16 per dtype). */
 int va_db_rows(const va_database* db, const void** rows);
 
+/* Ingestion (GPUVectorStorage write / ensureCapacity / compact, Index/Internal/
+ * GPUVectorStorage.swift:75-260): append `count` rows (the database's row format: dtype rows,
+ * or packed uint32 codes for a binary database) from host or device memory, growing capacity
+ * geometrically; overwrite rows [slot0, slot0 + count); keep only the rows whose keep[i] != 0
+ * (host array of the current row count), in order. Norms, tensor-core operands, int8 codes and a
+ * resident bit expansion are updated for the written rows. new_slot (optional, host, one per old
+ * row) receives each row's new index or -1. Stream-ordered; compaction waits for the stream. */
+int va_db_append(va_context* ctx, va_database* db, const void* rows, int on_device, int64_t count);
+int va_db_update(va_context* ctx, va_database* db, int64_t slot0, const void* rows, int on_device, int64_t count);
+int va_db_compact(va_context* ctx, va_database* db, const uint8_t* keep, int64_t* new_slot);
+
 /* Fused exact k-NN over the database: queries[nq x dim] fp32 (device), results sorted
  * best-first into out_vals/out_ids [nq x k] (device). Replaces FusedL2TopKKernel.execute
  * (Kernels/Metal4/FusedL2TopKKernel.swift:367-427) and the batch flat search

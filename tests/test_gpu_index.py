@@ -29,3 +29,23 @@ def test_index_filtered_search_matches_oracle(ctx, oracle):
     plain = idx.search(q[0], 5)
     want = [int(i) for i in tids[0] if int(i) not in (7, 507)][:5]
     assert [h.id.value for h in plain.results] == [hs[i].value for i in want]
+
+
+def test_index_device_ingestion_matches_rebuild(ctx, oracle):
+    """Inserts after the first search append on the device, compaction gathers on the device:
+    results equal a fresh index over the same live rows."""
+    import vectoraccelerate_b200 as va
+    x = oracle.gen_gaussian(4000, 32, 63)
+    q = oracle.gen_gaussian(5, 32, 64, row0=1 << 31)
+    idx = va.AcceleratedVectorIndex(va.IndexConfiguration.flat(32), ctx)
+    hs = idx.insert_batch(x[:1000])
+    idx.search(q[0], 3)  # creates the device database
+    hs += idx.insert_batch(x[1000:2500])
+    hs += idx.insert_batch(x[2500:])
+    idx.remove_batch(hs[::7])
+    idx.compact()
+    live = np.array([i for i in range(4000) if i % 7 != 0])
+    tids, _ = oracle.knn(q, x[live], 6)
+    got = idx.search_batch(q, 6)
+    for r in range(5):
+        assert [h.id.value for h in got[r].results] == [hs[live[i]].value for i in tids[r]]

@@ -64,6 +64,9 @@ SIGNATURES = {
     "va_topk_merge": [_P, _P, _P, _I, _P, _P, _I, _U32, _I64, _I, _P, _P],
     "va_merge_shards": [_P, _P, _P, _I, _I64, _I, _I, _P, _P],
     "va_db_create": [_P, _P, _I, _I64, _I, _I, _U32, _PP],
+    "va_db_append": [_P, _P, _P, _I, _I64],
+    "va_db_update": [_P, _P, _I64, _P, _I, _I64],
+    "va_db_compact": [_P, _P, _P, _P],
     "va_db_destroy": [_P],
     "va_db_info": [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I), ctypes.POINTER(_I)],
     "va_db_rows": [_P, _PP],

@@ -521,6 +521,26 @@ int hamming_chunked(va_context* ctx, va_database* db, const uint32_t* queries, i
 
 }  // namespace
 
+// Integer codes of rows [r0, r0 + count): per-dimension codes and |code|^2 of an int8 database,
+// or the 0/1 expansion and popcounts of a binary database whose expansion is resident. Used by
+// ingestion after rows were written.
+int va_db_derive_codes(va_context* ctx, va_database* db, int64_t r0, int64_t count) {
+    if (count <= 0) return VA_OK;
+    if (db->kind == VA_DB_INT8) {
+        k_perdim_codes<<<warps_grid(count), 256, 0, ctx->stream>>>((const float*)db->rows + r0 * db->dim, count, count,
+                                                                  db->dim, db->cpad, db->sq_mins, db->sq_scales,
+                                                                  db->codes + r0 * db->cpad, db->code_norms + r0);
+        return va_check_launch("k_perdim_codes(append)");
+    }
+    if (db->kind == VA_DB_BINARY && db->codes) {
+        k_expand_bits<<<warps_grid(count), 256, 0, ctx->stream>>>((const uint32_t*)db->rows + r0 * db->words, count,
+                                                                 count, db->words, db->cpad, db->codes + r0 * db->cpad,
+                                                                 db->code_norms + r0);
+        return va_check_launch("k_expand_bits(append)");
+    }
+    return VA_OK;
+}
+
 extern "C" {
 
 int va_sq_perdim_minmax(va_context* ctx, const float* x, int64_t n, int dim, float* out_min, float* out_max) {

@@ -103,6 +103,7 @@ struct va_database {
     int* stage_norms = nullptr;  // popcounts of the current chunk (padded to 256 rows)
     int64_t stage_rows = 0;      // rows per chunk (0: not chunked)
     int64_t chunk_request = 0;   // rows per chunk set by the caller (0: automatic)
+    int64_t cap = 0;             // rows allocated in every per-row array (0: exactly n)
 };
 
 #define VA_DB_FLOAT 0

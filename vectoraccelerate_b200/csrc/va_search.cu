@@ -821,6 +821,37 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
                            out_vals, out_ids);
 }
 
+// Derived per-row data of a float (or int8) database for rows [r0, r0 + count): row biases (and
+// the +inf pad after them up to a multiple of 256 rows) and every tensor-core operand already
+// built (aliases of the rows need nothing). Used by ingestion after rows were written.
+int va_db_derive_rows(va_context* ctx, va_database* db, int64_t r0, int64_t count) {
+    if (count <= 0) return VA_OK;
+    const size_t esz = db->dtype == VA_DTYPE_BF16 ? 2 : 4;
+    const void* src = (const uint8_t*)db->rows + (size_t)r0 * db->dim * esz;
+    // Rows past the database's end (up to a multiple of 256) get the +inf pad; rows inside it
+    // (an update in the middle) are left alone.
+    const int64_t pad_end = r0 + count >= db->n ? round_up(db->n, 256) : r0 + count;
+    if (db->norms2) {
+        k_row_bias<<<warps_grid(pad_end - r0), 256, 0, ctx->stream>>>(src, db->dtype, count, pad_end - r0, db->dim,
+                                                                      db->norms2 + r0, db->zbias + r0);
+        VA_TRY(va_check_launch("k_row_bias(append)"));
+    }
+    const int64_t dp = db->dpad;
+    if (db->op && !db->op_alias)
+        k_operand<uint16_t><<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, count, db->dim, db->dpad,
+                                                                        0, db->op + r0 * dp);
+    if (db->op_cos)
+        k_operand<uint16_t><<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, count, db->dim, db->dpad,
+                                                                        1, db->op_cos + r0 * dp);
+    if (db->op_f32 && !db->op_f32_alias)
+        k_operand<float><<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, count, db->dim, db->dpad,
+                                                                     0, db->op_f32 + r0 * dp);
+    if (db->op_f32_cos)
+        k_operand<float><<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, count, db->dim, db->dpad,
+                                                                     1, db->op_f32_cos + r0 * dp);
+    return va_check_launch("k_operand(append)");
+}
+
 // Internal entry of the merge + exact rerank step for other translation units (the int8 path).
 int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                              const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,

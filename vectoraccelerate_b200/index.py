@@ -10,8 +10,10 @@ until k results pass or every slot was seen, :1188-1265); ``search(queries:k:fil
 batches unfiltered queries in one GPU call. Distances are squared L2 (the reference's index is
 euclidean-only, :305-315); cosine and inner product are accepted here as an extension.
 
-Rows live in a resident device database that is rebuilt from the host mirror when inserts or
-compaction changed it (the reference's GPUVectorStorage writes through unified memory).
+Rows live in a resident device database created on the first search and then kept in step on
+the device: inserts append to it (va_db_append, geometric growth) and compaction gathers its kept
+rows (va_db_compact), as GPUVectorStorage writes and compacts its buffer. A host copy of the rows
+serves ``vector(for:)`` and the exhaustive tail of a filtered search.
 """
 
 from __future__ import annotations
@@ -89,7 +91,6 @@ class AcceleratedVectorIndex:
         self._metadata: dict[int, VectorMetadata] = {}
         self._next_handle = 0
         self._db: Database | None = None
-        self._dirty = True
 
     # ------------------------------------------------------------------------- mutation
     def insert(self, vector, metadata: Optional[VectorMetadata] = None) -> VectorHandle:
@@ -115,7 +116,8 @@ class AcceleratedVectorIndex:
             if metadata is not None and metadata[i] is not None:
                 self._metadata[h] = dict(metadata[i])
             handles.append(VectorHandle(h))
-        self._dirty = True
+        if self._db is not None:
+            self._db.append(v)
         return handles
 
     def remove(self, handle: VectorHandle) -> None:
@@ -139,11 +141,16 @@ class AcceleratedVectorIndex:
         if not self._deleted.any():
             return
         keep = ~self._deleted
+        if self._db is not None:
+            if keep.any():
+                self._db.compact(keep)
+            else:
+                self._db.close()
+                self._db = None
         self._rows = np.ascontiguousarray(self._rows[keep])
         self._slot_handle = [h for h, k in zip(self._slot_handle, keep) if k]
         self._handle_slot = {h: s for s, h in enumerate(self._slot_handle)}
         self._deleted = np.zeros(self._rows.shape[0], bool)
-        self._dirty = True
 
     def set_metadata(self, metadata: Optional[VectorMetadata], handle: VectorHandle) -> None:
         if handle.value not in self._handle_slot:
@@ -188,11 +195,8 @@ class AcceleratedVectorIndex:
 
     # ------------------------------------------------------------------------- search
     def _database(self) -> Database:
-        if self._dirty or self._db is None:
-            if self._db is not None:
-                self._db.close()
+        if self._db is None:
             self._db = Database(self.context, self._rows)
-            self._dirty = False
         return self._db
 
     def _fetch(self, q: np.ndarray, fetch_k: int):

@@ -247,6 +247,37 @@ class Database:
         _ffi.call("va_db_rows", self.handle, ctypes.byref(p))
         return p.value
 
+    def _row_array(self, rows):
+        a = np.ascontiguousarray(rows, dtype=np.uint16 if self.dtype == _ffi.DTYPE_BF16 else np.float32)
+        if a.ndim == 1:
+            a = a[None, :]
+        if a.shape[1] != self.dim:
+            raise InvalidInput(f"row dimension {a.shape[1]} != database dimension {self.dim}")
+        return a
+
+    def append(self, rows) -> None:
+        """Append rows (va_db_append): capacity grows geometrically, derived data is updated."""
+        a = self._row_array(rows)
+        _ffi.call("va_db_append", self.context.handle, self.handle, a.ctypes.data_as(_vp), 0, a.shape[0])
+        self.context.synchronize()
+        self.n += a.shape[0]
+
+    def update(self, slot0: int, rows) -> None:
+        """Overwrite rows [slot0, slot0 + len(rows)) (va_db_update)."""
+        a = self._row_array(rows)
+        _ffi.call("va_db_update", self.context.handle, self.handle, slot0, a.ctypes.data_as(_vp), 0, a.shape[0])
+        self.context.synchronize()
+
+    def compact(self, keep) -> np.ndarray:
+        """Keep rows where keep is true, in order (va_db_compact); returns old -> new slot (-1: dropped)."""
+        k = np.ascontiguousarray(keep, np.uint8)
+        if k.shape != (self.n,):
+            raise InvalidInput(f"keep must have one entry per row ({self.n})")
+        new_slot = np.empty(self.n, np.int64)
+        _ffi.call("va_db_compact", self.context.handle, self.handle, k.ctypes.data_as(_vp), new_slot.ctypes.data_as(_vp))
+        self.n = int((k != 0).sum())
+        return new_slot
+
     def close(self):
         if getattr(self, "handle", None):
             _ffi.call("va_db_destroy", self.handle)
