@@ -198,8 +198,11 @@ int va_db_compact(va_context* ctx, va_database* db, const uint8_t* keep, int64_t
  * best-first into out_vals/out_ids [nq x k] (device). Replaces FusedL2TopKKernel.execute
  * (Kernels/Metal4/FusedL2TopKKernel.swift:367-427) and the batch flat search
  * AcceleratedVectorIndex.searchBatchGPU (Index/AcceleratedVectorIndex.swift:1278-1374), extended
- * to cosine and inner product. rerank = candidate pool per query of the reduced-precision pass
- * (0 = automatic). */
+ * to cosine and inner product. rerank = candidate-pool factor of the reduced-precision pass
+ * (pool = rerank * k; 0 = automatic: k + max(k/4, 22), widened to 3k for bf16). The call is
+ * stream-ordered, except that a pool wider than 128 candidates reads back (and waits for) the
+ * count of queries whose pool could not be proven exact, which then take the FP32 route. A
+ * context serves one host thread at a time (its scratch buffers are shared by its calls). */
 int va_knn_search(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int metric,
                   int precision, int rerank, float* out_vals, uint32_t* out_ids);
 /* Same, with HOST query and result buffers: copies in, searches, copies out and waits (bounded).
@@ -265,7 +268,9 @@ int va_db_int8_params(const va_database* db, const float** mins, const float** s
  * best rows per query by (integer distance, id); those are reranked by exact squared L2 against
  * the fp32 rows (fp64 accumulation); out_vals/out_ids [nq x k] sorted by (distance, id). No
  * reference counterpart (the reference has quantizers only, DataTransformations.metal:142-221);
- * this is the search its int8 storage would feed (IVFQuantizedStorage.swift). */
+ * this is the search its int8 storage would feed (IVFQuantizedStorage.swift). candidates <= 4096;
+ * above 128 the call waits for the stream once (queries whose candidate set could not be proven
+ * from the filter's lists are recomputed by an exact integer scan). */
 int va_int8_knn_search(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int candidates,
                        float* out_vals, uint32_t* out_ids);
 
