@@ -203,6 +203,13 @@ __device__ __forceinline__ void tmem_wait64(uint32_t (&r)[64]) {
 // ids li[r*KP + j], j < KP, sorted by (key, id). The 32 lanes of a warp update one row's list
 // together: lane l holds entries l, l + 32, ... (E = KP / 32 per lane).
 //
+// Row stride of the candidate lists in shared memory: KP + 1 for KP <= 64, so that both one row
+// read by the whole warp (warp-cooperative insertion) and 32 rows read one entry each (per-lane
+// insertion) touch 32 different banks; 128-entry lists keep stride KP (no per-lane mode), their
+// shared memory being needed for pipeline stages.
+template <int KP>
+constexpr int list_stride() { return KP <= 64 ? KP + 1 : KP; }
+
 // Insert (key, id) into row r's list (warp-uniform arguments) and return the new KP-th key.
 // The position is the number of entries <= key (candidates arrive in increasing id order, so an
 // equal key goes after the entries already there: the (key, id) order); entries from the position
@@ -214,8 +221,8 @@ __device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r
     uint32_t ei[E];
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-        ek[k] = lk[r * KP + k * 32 + lane];
-        ei[k] = li[r * KP + k * 32 + lane];
+        ek[k] = lk[r * list_stride<KP>() + k * 32 + lane];
+        ei[k] = li[r * list_stride<KP>() + k * 32 + lane];
     }
     int pos = 0;
 #pragma unroll
@@ -238,14 +245,33 @@ __device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r
         if (p >= pos) {
             const float nk = p == pos ? key : pk;
             const uint32_t ni = p == pos ? id : pi;
-            lk[r * KP + p] = nk;
-            li[r * KP + p] = ni;
+            lk[r * list_stride<KP>() + p] = nk;
+            li[r * list_stride<KP>() + p] = ni;
             if (k == E - 1) last = nk;
         } else if (k == E - 1) {
             last = ek[k];
         }
     }
     return __shfl_sync(0xFFFFFFFFu, last, 31);
+}
+
+// Insert (key, id) into this lane's own row list (key below the row's KP-th key): entries
+// greater than key move up one slot from the end (the KP-th drops out), an equal key goes after
+// the entries already there. Returns the new KP-th key.
+template <int KP>
+__device__ __forceinline__ float lane_list_insert(float* lk, uint32_t* li, int r, float key, uint32_t id) {
+    float* k = lk + r * list_stride<KP>();
+    uint32_t* d = li + r * list_stride<KP>();
+    int p = KP - 1;
+    for (; p > 0; --p) {
+        const float prev = k[p - 1];
+        if (!(prev > key)) break;
+        k[p] = prev;
+        d[p] = d[p - 1];
+    }
+    k[p] = key;
+    d[p] = id;
+    return k[KP - 1];
 }
 
 // One 64-column chunk C (compile-time, so every shuffle reads a fixed register of a fixed lane).
@@ -287,6 +313,25 @@ __device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bi
     if (pass) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) kk[i] = __uint_as_float(r[i]);
+    }
+    if constexpr (list_stride<KP>() != KP) {
+        // Many candidates in the chunk (a cold list, or a dense pool): each lane inserts its own
+        // candidates into its own row in column order, all lanes at once.
+        const unsigned total = __reduce_add_sync(0xFFFFFFFFu, (unsigned)__popcll(pass));
+        if (total >= 8u) {
+            while (__any_sync(0xFFFFFFFFu, pass != 0)) {
+                if (pass) {
+                    const int i = __ffsll((long long)pass) - 1;
+                    pass &= pass - 1;
+                    const float key = kk[i];
+                    if (key < thr && id0 + (uint32_t)i < n_rows) {
+                        thr_own = lane_list_insert<KP>(lk, li, row0 + lane, key, id0 + (uint32_t)i);
+                        thr = fminf(thr_own, thr_g);
+                    }
+                }
+            }
+            return;
+        }
     }
     for (;;) {
         const uint32_t lanes = __ballot_sync(0xFFFFFFFFu, pass != 0);
@@ -425,9 +470,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)stages * A_BYTES;
-    float* l_key = (float*)(sB + (size_t)stages * B_BYTES);       // [KP][BM]
-    uint32_t* l_id = (uint32_t*)(l_key + KP * BM);                 // [KP][BM]
-    uint64_t* bars = (uint64_t*)(l_id + KP * BM);                  // full[stages], empty[stages], tfull[2], tempty[2]
+    float* l_key = (float*)(sB + (size_t)stages * B_BYTES);       // [BM][stride]
+    uint32_t* l_id = (uint32_t*)(l_key + list_stride<KP>() * BM);  // [BM][stride]
+    uint64_t* bars = (uint64_t*)(l_id + list_stride<KP>() * BM);                  // full[stages], empty[stages], tfull[2], tempty[2]
     uint64_t* full = bars;
     uint64_t* empty = bars + stages;
     uint64_t* tfull = bars + 2 * stages;
@@ -549,9 +594,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             item_range(w, item, qt, t0, t1);
             const int64_t q = (int64_t)qt * BM + row;
             // Reset this warp's 32 row lists (row-contiguous, KP entries each; coalesced).
-            for (int e = lane; e < 32 * KP; e += 32) {
-                l_key[quarter * 32 * KP + e] = INFINITY;
-                l_id[quarter * 32 * KP + e] = va::kInvalidId;
+            for (int e = lane; e < 32 * list_stride<KP>(); e += 32) {
+                l_key[quarter * 32 * list_stride<KP>() + e] = INFINITY;
+                l_id[quarter * 32 * list_stride<KP>() + e] = va::kInvalidId;
             }
             __syncwarp();
             const int qn = row_qn ? row_qn[q] : 0;
@@ -565,7 +610,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             const int split = item / w.n_qtiles;
-            const float* const row_keys = l_key + (size_t)row * KP;
+            const float* const row_keys = l_key + (size_t)row * list_stride<KP>();
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 3) == 3) {
                     publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
@@ -620,8 +665,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // ([split][query][KP]): copy them with coalesced stores.
                 const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
-                    part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
-                    part_ids[out0 + e] = l_id[quarter * 32 * KP + e];
+                    const int src = (quarter * 32 + e / KP) * list_stride<KP>() + e % KP;
+                    part_keys[out0 + e] = l_key[src];
+                    part_ids[out0 + e] = l_id[src];
                 }
                 __syncwarp();
             }
@@ -752,9 +798,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)stages * PA_BYTES;
-    float* l_key = (float*)(sB + (size_t)stages * PB_BYTES);  // [128][KP]
-    uint32_t* l_id = (uint32_t*)(l_key + KP * P_ROWS);          // [128][KP]
-    uint64_t* bars = (uint64_t*)(l_id + KP * P_ROWS);
+    float* l_key = (float*)(sB + (size_t)stages * PB_BYTES);  // [128][stride]
+    uint32_t* l_id = (uint32_t*)(l_key + list_stride<KP>() * P_ROWS);  // [128][stride]
+    uint64_t* bars = (uint64_t*)(l_id + list_stride<KP>() * P_ROWS);
     uint64_t* full = bars;
     uint64_t* empty = bars + stages;
     uint64_t* tfull = bars + 2 * stages;
@@ -878,9 +924,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             item_range(w, item, qt, t0, t1);
             const int64_t qbase = (int64_t)qt * PBM + (int64_t)rank * P_ROWS;
             const int64_t q = qbase + row;
-            for (int e = lane; e < 32 * KP; e += 32) {
-                l_key[quarter * 32 * KP + e] = INFINITY;
-                l_id[quarter * 32 * KP + e] = va::kInvalidId;
+            for (int e = lane; e < 32 * list_stride<KP>(); e += 32) {
+                l_key[quarter * 32 * list_stride<KP>() + e] = INFINITY;
+                l_id[quarter * 32 * list_stride<KP>() + e] = va::kInvalidId;
             }
             __syncwarp();
             const int qn = row_qn ? row_qn[q] : 0;
@@ -892,7 +938,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
             const int split = item / w.n_qtiles;
-            const float* const row_keys = l_key + (size_t)row * KP;
+            const float* const row_keys = l_key + (size_t)row * list_stride<KP>();
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 3) == 3) {
                     publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
@@ -941,8 +987,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
                 const int64_t out0 = ((int64_t)s * w.nq_pad + qbase + quarter * 32) * KP;
                 for (int e = lane; e < 32 * KP; e += 32) {
-                    part_keys[out0 + e] = l_key[quarter * 32 * KP + e];
-                    part_ids[out0 + e] = l_id[quarter * 32 * KP + e];
+                    const int src = (quarter * 32 + e / KP) * list_stride<KP>() + e % KP;
+                    part_keys[out0 + e] = l_key[src];
+                    part_ids[out0 + e] = l_id[src];
                 }
                 __syncwarp();
             }
@@ -1022,8 +1069,9 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
 }
 
 size_t smem_bytes(int kp, int stages, bool pair) {
-    return 1024 + (size_t)stages * (pair ? PSTAGE_BYTES : STAGE_BYTES) + (size_t)kp * BM * 8 + (2 * stages + 4) * 8 +
-           16;
+    const int stride = kp <= 64 ? kp + 1 : kp;  // list_stride<KP>()
+    return 1024 + (size_t)stages * (pair ? PSTAGE_BYTES : STAGE_BYTES) + (size_t)stride * BM * 8 +
+           (2 * stages + 4) * 8 + 16;
 }
 
 }  // namespace
