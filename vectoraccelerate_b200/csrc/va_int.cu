@@ -467,7 +467,7 @@ namespace {
 int hamming_view(va_context* ctx, const va_database* view, const uint32_t* queries, int64_t nq, int k, float* out_v,
                  uint32_t* out_i) {
     TcPlan plan;
-    VA_TRY(va_tc_plan_pool(ctx, nq, view->n, k, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, view->n, k, &plan, view->cpad));
     IntScratch s;
     VA_TRY(int_scratch(ctx, view, plan, &s));
     k_expand_bits<<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(queries, nq, plan.nq_pad, view->words, view->cpad,
@@ -630,7 +630,7 @@ int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* que
     va_database* db = const_cast<va_database*>(cdb);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     TcPlan plan;
-    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, candidates, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, candidates, &plan, db->cpad));
     IntScratch s;
     VA_TRY(int_scratch(ctx, db, plan, &s));
     uint32_t *fail_cnt = nullptr, *fail_list = nullptr, *gi = nullptr;
@@ -786,7 +786,7 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
     }
     if (!db->codes) return hamming_chunked(ctx, db, queries, nq, k, out_dists, out_ids);
     TcPlan plan;
-    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, k, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, k, &plan, db->cpad));
     IntScratch s;
     VA_TRY(int_scratch(ctx, db, plan, &s));
     void* ws2;

@@ -399,7 +399,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
               int pool, float* out_vals, uint32_t* out_ids) {
     const bool wide = pool > 128;
     TcPlan plan;
-    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, pool, &plan));
+    VA_TRY(va_tc_plan_pool(ctx, nq, db->n, pool, &plan, (int64_t)db->dpad * elem));
     const int kp = plan.kp;  // list length (up to 128 the whole list is the pool)
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = nullptr;
@@ -743,7 +743,7 @@ int noalloc_scratch(int device, void** out) {
 int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
                     int kp, uint8_t* scratch, size_t scratch_bytes, float* out_vals, uint32_t* out_ids) {
     TcPlan plan;
-    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan));
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan, (int64_t)db->dpad * elem));
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = elem == 2 ? (cosine ? (const void*)db->op_cos : (const void*)db->op)
                                  : (cosine ? (const void*)db->op_f32_cos : (const void*)db->op_f32);

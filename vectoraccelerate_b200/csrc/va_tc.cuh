@@ -54,8 +54,9 @@ struct TcFilterArgs {
                           // slots * rank must be at least the final pool (kp when the pool is the list)
 };
 
-int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan);
-int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPlan* plan);
+// row_bytes: bytes of one operand row (dpad x element size), which sets the time of a tile.
+int va_tc_plan(va_context* ctx, int64_t nq, int64_t n_rows, int kp, TcPlan* plan, int64_t row_bytes = 1536);
+int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPlan* plan, int64_t row_bytes = 1536);
 int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
 int va_tc_stages(int kp, bool pair);
 bool va_tc_use_pair();
