@@ -11,17 +11,17 @@
 //                 4 tcgen05.mma per K block into the current accumulator, tcgen05.commit frees
 //                 the slot; a final commit hands the accumulator to the epilogue
 //   warps 2..5    epilogue: tcgen05.ld 64 columns at a time (one query row per thread, loads
-//                 double-buffered), forms key = alpha * (q.x) + row bias (|x|^2 for L2) with the
-//                 biases broadcast by shuffles, and keeps a sorted list of each query's KP best
-//                 (key, id) in shared memory. A warp-uniform test per 64-column chunk skips the
-//                 lists; otherwise the warp inserts the passing candidates one at a time, all 32
-//                 lanes updating one list (position by ballot, shift by shuffle)
+//                 double-buffered), forms key = alpha * (q.x) + row bias (|x|^2 for L2; the
+//                 exact integer distance for int8 / bit codes) with the biases broadcast by
+//                 shuffles, and keeps a sorted list of each query's KP best (key, id) in shared
+//                 memory. A warp-uniform test per 64-column chunk skips the lists; otherwise the
+//                 candidates are inserted one at a time by the whole warp (few candidates) or by
+//                 every lane into its own row at once (many)
 //
 // Every (query tile, row split) item starts its lists empty, so without help each item would
-// re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share one bound per
-// query in global memory: a finished item publishes its KP-th key (atomicMin on the orderable
-// key); others drop keys above the smallest published bound. The bound is the KP-th key of a
-// subset of rows, never below the global KP-th key, so no candidate of the final pool is lost.
+// re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share a bound per
+// query in global memory, in levels of slots fed with list keys of several ranks (see
+// Work::lv); keys above it are dropped, and it never cuts into the final candidate pool.
 //
 // The producers of all CTAs advance through row chunks in loose lockstep (each CTA at most two
 // 16-tile chunks ahead of the slowest), so the 2-3 row splits in flight stay in L2 and each row is
