@@ -79,6 +79,7 @@ extern "C" {
 
 typedef struct va_context va_context;
 typedef struct va_database va_database;
+typedef struct va_ivf va_ivf;
 
 /* Context configuration (Metal4Configuration, Core/Metal4Context.swift:13-44). */
 typedef struct va_config {
@@ -305,6 +306,39 @@ int va_db_binary_set_chunk_rows(va_database* db, int64_t rows);
  * HammingDistanceKernel.swift:114-120,313-363). out_dists may be NULL. */
 int va_hamming_knn_db(va_context* ctx, const va_database* db, const uint32_t* queries, int64_t nq, int k,
                       uint32_t* out_dists, uint32_t* out_ids);
+
+/* ------------------------------------------------------------------------------------------ */
+/* IVF index (IVFSearchPipeline, Index/Kernels/IVF/IVFSearchPipeline.swift:110-600; k-means      */
+/* training, Index/Kernels/Clustering/KMeansPipeline.swift:102-240). Squared L2, fp32 rows.     */
+/* ------------------------------------------------------------------------------------------ */
+/* k-means over x[n x dim] (device): initial centroids are nlist distinct rows drawn with `seed`
+ * (or, with init_given != 0, the centroids out_centroids holds on entry), then Lloyd iterations
+ * (exact assignment, mean update; an empty list keeps its centroid) until the largest centroid
+ * movement is below tol or max_iters iterations ran. out_centroids [nlist x dim] (device);
+ * out_iters (host, optional) = iterations run. */
+int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist, int max_iters, float tol,
+                 uint64_t seed, int init_given, float* out_centroids, int* out_iters);
+/* Build the inverted lists: every row of rows[n x dim] (device) goes to its nearest centroid
+ * (ties to the lower list), rows are copied in list order (stable within a list), ids are
+ * row + id_base (IVFSearchPipeline.prepareIndexStructure, :110-195). */
+int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const float* centroids, int nlist,
+                  uint32_t id_base, va_ivf** out);
+/* The same from lists the caller has already formed (IVFSearchPipeline.prepareIndexStructure
+ * with explicit lists, :110-185): centroids [nlist x dim], rows [offsets[nlist] x dim] in list
+ * order, offsets [nlist + 1] (HOST, offsets[0] = 0), ids [offsets[nlist]] or NULL for the
+ * position in the concatenated lists (the reference's vector index). centroids, rows and ids are
+ * host (on_device = 0) or device (1) memory. */
+int va_ivf_create_lists(va_context* ctx, const float* centroids, int nlist, int dim, const float* rows,
+                        const int64_t* offsets, const uint32_t* ids, int on_device, va_ivf** out);
+int va_ivf_destroy(va_ivf* ivf);
+/* Rows per list (host array of nlist). */
+int va_ivf_list_sizes(const va_ivf* ivf, int64_t* sizes);
+/* Approximate k-NN (IVFSearchPipeline.search, :197-570): each query's nprobe nearest centroids
+ * (exact, ties by list id), then the exact squared L2 to every row of those lists; the k best
+ * by (distance, id), sorted best-first; missing results are (+inf, 0xFFFFFFFF). queries [nq x
+ * dim], outputs [nq x k], all device; k <= 128, nq <= 65535. */
+int va_ivf_search(va_context* ctx, const va_ivf* ivf, const float* queries, int64_t nq, int k, int nprobe,
+                  float* out_vals, uint32_t* out_ids);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Seeded synthetic data on the device (restates Tests/.../Utilities/TestRNG.swift:57-161;     */

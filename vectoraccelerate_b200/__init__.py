@@ -11,6 +11,8 @@ from ._ffi import (DTYPE_BF16, DTYPE_F32, INVALID_ID, METRIC_COSINE, METRIC_IP, 
 from .context import DeviceBuffer, GPUContext, Metal4Configuration, Metal4Context
 from .errors import (BufferAllocationFailed, CollectiveFailed, ComputeFailed, InvalidInput, Timeout, Unsupported,
                      VectorError)
+from .ivf import (IVFGPUIndexStructure, IVFSearchConfiguration, IVFSearchPipeline, IVFSearchResult,
+                  KMeansConfiguration, KMeansPipeline, KMeansResult)
 from .index import AcceleratedVectorIndex, IndexConfiguration, IndexSearchResult, SearchResults, VectorHandle
 from .provider import MetalComputeProvider
 from .kernels import (BinaryDatabase, BinaryQuantizationKernel, CosineSimilarityKernel, Database, DotProductKernel,

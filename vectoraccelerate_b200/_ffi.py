@@ -88,6 +88,12 @@ SIGNATURES = {
     "va_db_create_binary": [_P, _P, _I, _I64, _I, _U32, _PP],
     "va_db_binary_set_chunk_rows": [_P, _I64],
     "va_hamming_knn_db": [_P, _P, _P, _I64, _I, _P, _P],
+    "va_ivf_train": [_P, _P, _I64, _I, _I, _I, _F, _U64, _I, _P, _P],
+    "va_ivf_create": [_P, _P, _I64, _I, _P, _I, _U32, _PP],
+    "va_ivf_create_lists": [_P, _P, _I, _I, _P, _P, _P, _I, _PP],
+    "va_ivf_destroy": [_P],
+    "va_ivf_list_sizes": [_P, _P],
+    "va_ivf_search": [_P, _P, _P, _I64, _I, _I, _P, _P],
     "va_gen_gaussian": [_P, _P, _I64, _I, _U64, _I64],
     "va_gen_mixture": [_P, _P, _I64, _I, _U64, _I64, _I, _F, _I],
     "va_f32_to_bf16": [_P, _P, _I64, _P],
