@@ -334,11 +334,19 @@ int va_ivf_destroy(va_ivf* ivf);
 /* Rows per list (host array of nlist). */
 int va_ivf_list_sizes(const va_ivf* ivf, int64_t* sizes);
 /* Approximate k-NN (IVFSearchPipeline.search, :197-570): each query's nprobe nearest centroids
- * (exact, ties by list id), then the exact squared L2 to every row of those lists; the k best
- * by (distance, id), sorted best-first; missing results are (+inf, 0xFFFFFFFF). queries [nq x
- * dim], outputs [nq x k], all device; k <= 128, nq <= 65535. */
+ * (ties by list id), then the k best rows of those lists by exact squared L2 and (distance, id),
+ * sorted best-first; missing results are (+inf, 0xFFFFFFFF). queries [nq x dim], outputs
+ * [nq x k], all device; k <= 128. For k <= 42 the lists are scanned on the tensor cores (the
+ * queries of each list gathered into tiles of 128, bf16 keys, a per-query bound shared by its
+ * probes) and a pool of max(3k, k + 22) candidates is reranked exactly; the tile layout is read
+ * back (the call waits for the coarse step). Larger k: an exact fp64 scan, nq <= 65535. The
+ * index keeps one search scratch: one search at a time per index. */
 int va_ivf_search(va_context* ctx, const va_ivf* ivf, const float* queries, int64_t nq, int k, int nprobe,
                   float* out_vals, uint32_t* out_ids);
+/* Same with HOST query and result buffers (copies in, searches, copies out, waits). The whole
+ * reference call IVFSearchPipeline.search(queries:structure:k:). */
+int va_ivf_search_host(va_context* ctx, const va_ivf* ivf, const float* queries_host, int64_t nq, int k, int nprobe,
+                       float* out_vals_host, uint32_t* out_ids_host);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Seeded synthetic data on the device (restates Tests/.../Utilities/TestRNG.swift:57-161;     */

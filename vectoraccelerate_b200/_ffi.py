@@ -94,6 +94,7 @@ SIGNATURES = {
     "va_ivf_destroy": [_P],
     "va_ivf_list_sizes": [_P, _P],
     "va_ivf_search": [_P, _P, _P, _I64, _I, _I, _P, _P],
+    "va_ivf_search_host": [_P, _P, _P, _I64, _I, _I, _P, _P],
     "va_gen_gaussian": [_P, _P, _I64, _I, _U64, _I64],
     "va_gen_mixture": [_P, _P, _I64, _I, _U64, _I64, _I, _F, _I],
     "va_f32_to_bf16": [_P, _P, _I64, _P],

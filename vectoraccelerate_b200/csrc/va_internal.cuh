@@ -172,13 +172,15 @@ struct SelectShared {
     int need;
     int done;
     int count;
+    int count_eq;
 };
 
 // Block-wide exact selection of the `want` smallest 64-bit composite keys among n candidates
-// given by get(i), i < n. Composites are unique (the low 32 bits carry the id), so the
-// want-th smallest is unique and the selection has exactly min(want, n) elements. They are
-// written unsorted to out[0 .. min(want,n)). Radix passes of 8 bits from the top; a pass stops
-// early once every element with the current prefix is needed.
+// given by get(i), i < n; the selection has exactly min(want, n) elements, written unsorted to
+// out[0 .. min(want,n)). Radix passes of 8 bits from the top; a pass stops early once every
+// element with the current prefix is needed. Composites are unique (the low 32 bits carry the
+// id) except the padding value ~0, which may repeat: the elements below the final prefix are all
+// taken and the ones equal to it only fill the remaining slots.
 template <class Get>
 __device__ int block_select_radix(int64_t n, int want, Get get, uint64_t* out, SelectShared& sh) {
     if (n <= want) {
@@ -194,6 +196,7 @@ __device__ int block_select_radix(int64_t n, int want, Get get, uint64_t* out, S
         sh.need = want;
         sh.done = 0;
         sh.count = 0;
+        sh.count_eq = 0;
     }
     __syncthreads();
     for (int shift = 56; shift >= 0; shift -= 8) {
@@ -246,11 +249,18 @@ __device__ int block_select_radix(int64_t n, int want, Get get, uint64_t* out, S
         if (sh.done) break;
     }
     const unsigned long long prefix = sh.prefix, mask = sh.mask;
+    // want - need elements lie below the prefix (front slots); `need` of those equal to it fill
+    // the back slots.
+    const int need = sh.need;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
         uint64_t c = get(i);
-        if ((c & mask) <= prefix) {
+        const unsigned long long m = c & mask;
+        if (m < prefix) {
             int slot = atomicAdd(&sh.count, 1);
             if (slot < want) out[slot] = c;
+        } else if (m == prefix) {
+            int slot = atomicAdd(&sh.count_eq, 1);
+            if (slot < need) out[want - 1 - slot] = c;
         }
     }
     __syncthreads();

@@ -18,7 +18,10 @@
 #include <cstring>
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "va_internal.cuh"
+#include "va_tc.cuh"
 
 extern "C" int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* ids, int nlists,
                                        int64_t list_stride, int len, int64_t nq, int k, int mode, float* out_vals,
@@ -35,6 +38,14 @@ struct va_ivf {
     uint32_t* ids = nullptr;       // [n] original id of each row in list order
     int64_t* offsets = nullptr;    // [nlist + 1] device
     std::vector<int64_t> h_offsets;
+    // Tensor-core operand of the rows in list order: bf16 [n x dpad] (zero padded), and the row
+    // biases |x|^2 for n + 512 rows (+inf past n: a list's last tile may reach 255 rows beyond it).
+    int dpad = 0;
+    uint16_t* op = nullptr;
+    float* bias = nullptr;
+    // Search scratch, grown on demand (one search at a time per index).
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
 };
 
 namespace {
@@ -150,6 +161,111 @@ __global__ void k_place_rows(const float* __restrict__ x, int64_t n, int dim, co
     for (int j = lane; j < dim; j += 32) rows_out[o * dim + j] = x[r * dim + j];
 }
 
+// out[r] = bf16 of src row map(r) zero padded to dpad (a zero row when map(r) < 0). map = null:
+// row r; else row map[r] / map_div (gathered (query, probe) pairs -> their query).
+__global__ void k_rows_bf16(const float* __restrict__ src, int64_t n_out, int dim, int dpad,
+                            const int* __restrict__ map, int map_div, uint16_t* __restrict__ out) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_out * dpad;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / dpad;
+        const int j = (int)(e - r * dpad);
+        int64_t sr = r;
+        if (map) sr = map[r] >= 0 ? map[r] / map_div : -1;
+        const float v = (sr >= 0 && j < dim) ? src[sr * dim + j] : 0.f;
+        out[e] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
+}
+
+// bias[r] = |x_r|^2 (fp64 sum, rounded) for r < n; +inf for n <= r < n_alloc. A warp per row.
+__global__ void k_row_norms(const float* __restrict__ x, int64_t n, int dim, int64_t n_alloc, float* __restrict__ bias) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_alloc) return;
+    if (r >= n) {
+        if (lane == 0) bias[r] = INFINITY;
+        return;
+    }
+    double s = 0;
+    for (int j = lane; j < dim; j += 32) {
+        const double v = x[r * dim + j];
+        s += v * v;
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) bias[r] = (float)s;
+}
+
+// cnt[L * nprobe + s] = pairs of probe rank s (the s-th nearest centroid) that fall on list L.
+__global__ void k_probe_hist(const uint32_t* __restrict__ probes, int64_t m, int nprobe, int* __restrict__ cnt) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
+        atomicAdd(cnt + (int64_t)probes[i] * nprobe + (int)(i % nprobe), 1);
+}
+
+// Every (query, probe) pair takes a row of its list's query tiles, the list's pairs ordered by
+// probe rank: position p = base[L, s] + arrival within (L, s), in tile tile_of[lt0[L] + p / 128]
+// at row p % 128. gmap[g] = pair, ginv[pair] = g.
+__global__ void k_probe_scatter(const uint32_t* __restrict__ probes, int64_t m, int nprobe,
+                                const int* __restrict__ base, int* __restrict__ cursor, const int* __restrict__ lt0,
+                                const int* __restrict__ tile_of, int* __restrict__ gmap, int64_t* __restrict__ ginv) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t ls = (int64_t)probes[i] * nprobe + (int)(i % nprobe);
+        const int p = base[ls] + atomicAdd(cursor + ls, 1);
+        const int64_t g = (int64_t)tile_of[lt0[probes[i]] + p / 128] * 128 + p % 128;
+        gmap[g] = (int)i;
+        ginv[i] = g;
+    }
+}
+
+// One block per query: the `pool` best approximate keys among its nprobe lists of kp candidates
+// (positions in list order), their exact squared L2 (fp64 of the fp32 rows), the k best by
+// (distance, original id), sorted.
+constexpr int MR_THREADS = 256;
+__global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __restrict__ q, int dim,
+                                                                 const int64_t* __restrict__ ginv, int nprobe,
+                                                                 const float* __restrict__ pk,
+                                                                 const uint32_t* __restrict__ pi, int kp, int pool,
+                                                                 int k, const float* __restrict__ rows,
+                                                                 const uint32_t* __restrict__ ids,
+                                                                 float* __restrict__ out_v,
+                                                                 uint32_t* __restrict__ out_i) {
+    __shared__ uint64_t s_sel[128];
+    __shared__ uint64_t s_ex[128];
+    __shared__ va::SelectShared sh;
+    const int64_t qi = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    auto get = [&](int64_t i) -> uint64_t {
+        const int s = (int)(i / kp), j = (int)(i - (int64_t)s * kp);
+        const int64_t o = ginv[qi * nprobe + s] * kp + j;
+        const uint32_t id = pi[o];
+        if (id == va::kInvalidId) return ~0ull;
+        return va::composite(va::f2key(pk[o]), id);
+    };
+    const int m = va::block_select_radix((int64_t)nprobe * kp, pool, get, s_sel, sh);
+    __syncthreads();
+    for (int c = warp; c < m; c += MR_THREADS / 32) {
+        const uint64_t sc = s_sel[c];
+        uint64_t comp = ~0ull;
+        if (sc != ~0ull) {
+            const uint32_t pos = (uint32_t)sc;
+            double acc = 0;
+            for (int j = lane; j < dim; j += 32) {
+                const double t = (double)q[qi * dim + j] - (double)rows[(int64_t)pos * dim + j];
+                acc += t * t;
+            }
+            acc = warp_sum_d(acc);
+            comp = va::composite(va::f2key((float)acc), ids[pos]);
+        }
+        if (lane == 0) s_ex[c] = comp;
+    }
+    const int p2 = va::next_pow2(m > 0 ? m : 1);
+    for (int i = m + threadIdx.x; i < p2; i += blockDim.x) s_ex[i] = ~0ull;
+    va::block_bitonic_sort(s_ex, p2);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const uint64_t c = i < m ? s_ex[i] : ~0ull;
+        out_v[qi * k + i] = c == ~0ull ? INFINITY : va::key2f((uint32_t)(c >> 32));
+        out_i[qi * k + i] = c == ~0ull ? va::kInvalidId : (uint32_t)c;
+    }
+}
+
 // ---------------------------------------------------------------------------------- list scan
 constexpr int LS_THREADS = 256;
 constexpr int LS_BUF = 1024;
@@ -228,6 +344,48 @@ __global__ void __launch_bounds__(LS_THREADS) k_ivf_scan(const float* __restrict
         out_v[o + i] = c == ~0ull ? INFINITY : va::key2f((uint32_t)(c >> 32));
         out_i[o + i] = c == ~0ull ? va::kInvalidId : (uint32_t)c;
     }
+}
+
+// The bf16 operand and row biases of the rows in list order.
+int prepare_operand(va_context* ctx, va_ivf* ivf) {
+    ivf->dpad = (int)round_up(ivf->dim, 64);
+    const int64_t n = ivf->n;
+    cudaError_t e = cudaMalloc((void**)&ivf->op, (size_t)std::max<int64_t>(n, 1) * ivf->dpad * 2);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&ivf->bias, (size_t)(n + 512) * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return va_set_error(VA_ERR_OOM, "IVF operand allocation failed: %s", cudaGetErrorString(e));
+    }
+    if (n) {
+        k_rows_bf16<<<grid_for(n * ivf->dpad), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, ivf->dpad, nullptr, 1,
+                                                                       ivf->op);
+        VA_TRY(va_check_launch("k_rows_bf16"));
+    }
+    k_row_norms<<<(unsigned)(((n + 512) * 32 + 255) / 256), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, n + 512,
+                                                                                  ivf->bias);
+    VA_TRY(va_check_launch("k_row_norms"));
+    return va_synchronize(ctx);
+}
+
+// The index's search scratch, at least `bytes`; when it grows, its first `keep` bytes move along.
+int scratch(va_context* ctx, va_ivf* ivf, size_t bytes, size_t keep, void** out) {
+    if (bytes > ivf->scratch_bytes) {
+        const size_t want = std::max(bytes, (size_t)1 << 20);
+        void* fresh = nullptr;
+        if (cudaMalloc(&fresh, want) != cudaSuccess) {
+            cudaGetLastError();
+            return va_set_error(VA_ERR_OOM, "IVF search scratch of %zu bytes failed", want);
+        }
+        if (ivf->scratch) {
+            if (keep) VA_CUDA_TRY(cudaMemcpyAsync(fresh, ivf->scratch, keep, cudaMemcpyDeviceToDevice, ctx->stream));
+            VA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+            cudaFree(ivf->scratch);
+        }
+        ivf->scratch = fresh;
+        ivf->scratch_bytes = want;
+    }
+    *out = ivf->scratch;
+    return VA_OK;
 }
 
 // Assignment of every row to its nearest centroid (the fused search with k = 1).
@@ -397,6 +555,7 @@ int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const 
     }
     if (st == VA_OK) st = va_synchronize(ctx);
     cudaFree(ws);
+    if (st == VA_OK) st = prepare_operand(ctx, ivf);
     if (st != VA_OK) return fail(st);
     *out = ivf;
     return VA_OK;
@@ -451,6 +610,7 @@ int va_ivf_create_lists(va_context* ctx, const float* centroids, int nlist, int 
     if (e != cudaSuccess) return fail(va_set_error(VA_ERR_CUDA, "IVF upload failed: %s", cudaGetErrorString(e)));
     int st = va_synchronize(ctx);
     if (st == VA_OK) st = va_db_create(ctx, ivf->centroids, 1, nlist, dim, VA_DTYPE_F32, 0, &ivf->cdb);
+    if (st == VA_OK) st = prepare_operand(ctx, ivf);
     if (st != VA_OK) return fail(st);
     *out = ivf;
     return VA_OK;
@@ -465,6 +625,9 @@ int va_ivf_destroy(va_ivf* ivf) {
     if (ivf->rows) cudaFree(ivf->rows);
     if (ivf->ids) cudaFree(ivf->ids);
     if (ivf->offsets) cudaFree(ivf->offsets);
+    if (ivf->op) cudaFree(ivf->op);
+    if (ivf->bias) cudaFree(ivf->bias);
+    if (ivf->scratch) cudaFree(ivf->scratch);
     delete ivf;
     return VA_OK;
 }
@@ -475,31 +638,169 @@ int va_ivf_list_sizes(const va_ivf* ivf, int64_t* sizes) {
     return VA_OK;
 }
 
-int va_ivf_search(va_context* ctx, const va_ivf* ivf, const float* queries, int64_t nq, int k, int nprobe,
+int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int64_t nq, int k, int nprobe,
                   float* out_vals, uint32_t* out_ids) {
-    VA_REQUIRE(ctx && ivf && queries && out_vals && out_ids, "all pointers must be non-NULL");
+    VA_REQUIRE(ctx && civf && queries && out_vals && out_ids, "all pointers must be non-NULL");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(k > 0 && k <= 128, "k must be between 1 and 128 for the IVF search, got %d", k);
-    VA_REQUIRE(nprobe > 0 && nprobe <= ivf->nlist, "nprobe must be in 1..nlist (%d), got %d", ivf->nlist, nprobe);
-    VA_REQUIRE(nq <= 65535, "numQueries %lld exceeds 65535 per IVF call", (long long)nq);
+    VA_REQUIRE(nprobe > 0 && nprobe <= civf->nlist, "nprobe must be in 1..nlist (%d), got %d", civf->nlist, nprobe);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
-    void* aux;
-    const size_t pb = round_up(nq * nprobe * 4, 256);
-    const size_t lb = (size_t)nprobe * nq * k;
-    VA_TRY(va_aux_buffer(ctx, 2 * pb + lb * 8 + 256, &aux));
-    uint32_t* probes = (uint32_t*)aux;
-    float* pv = (float*)((uint8_t*)aux + pb);
-    float* cv = (float*)((uint8_t*)aux + 2 * pb);
-    uint32_t* ci = (uint32_t*)(cv + lb);
-    // Coarse quantization: the nprobe nearest centroids of every query (exact, (distance, id)).
-    VA_TRY(va_knn_search(ctx, ivf->cdb, queries, nq, nprobe, VA_METRIC_L2SQ, VA_PREC_AUTO, 0, pv, probes));
-    const size_t smem = (size_t)ivf->dim * 4;
-    if (smem > 48 * 1024) VA_CUDA_TRY(cudaFuncSetAttribute(k_ivf_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((unsigned)nprobe, (unsigned)nq);
-    k_ivf_scan<<<grid, LS_THREADS, smem, ctx->stream>>>(queries, nq, ivf->dim, probes, nprobe, ivf->rows, ivf->ids,
-                                                       ivf->offsets, k, cv, ci);
-    VA_TRY(va_check_launch("k_ivf_scan"));
-    return va_merge_lists_internal(ctx, cv, ci, nprobe, nq * k, k, nq, k, VA_SELECT_MIN, out_vals, out_ids);
+    va_ivf* ivf = const_cast<va_ivf*>(civf);  // only its search scratch changes
+    const int64_t m = nq * nprobe;
+    // Candidate pool of the tensor-core route: as the flat search's bf16 pool (3k, at least
+    // k + max(k/4, 22)); up to 128 it fits one list per (query, probe). Larger k: the exact scan.
+    const int pool = std::max(3 * k, k + std::max(k / 4, 22));
+    const bool tc = pool <= 128 && ivf->n > 0;
+    const int kp = pool <= 32 ? 32 : pool <= 64 ? 64 : 128;
+    const int nlist = ivf->nlist;
+    // Scratch: probes + their distances, then the route's arrays (sized after the plan).
+    const size_t pb = round_up(m * 4, 256);
+    void* ws;
+    const size_t head = 2 * pb + round_up((int64_t)nlist * nprobe * 4, 256);
+    VA_TRY(scratch(ctx, ivf, head, 0, &ws));
+    uint32_t* probes = (uint32_t*)ws;
+    float* pv = (float*)((uint8_t*)ws + pb);
+    int* cnt = (int*)((uint8_t*)ws + 2 * pb);
+    // Coarse quantization: the nprobe nearest centroids of every query (exact, ties by list id).
+    // TF32 with the default pool nprobe + max(nprobe / 4, 22) keeps lists of at most 128 on the
+    // single-CTA kernel (few centroids, many queries); tiny dimensions and wide pools: automatic.
+    const int cprec = (ivf->dim > 16 && nprobe + std::max(nprobe / 4, 22) <= 128) ? VA_PREC_TF32 : VA_PREC_AUTO;
+    VA_TRY(va_knn_search(ctx, ivf->cdb, queries, nq, nprobe, VA_METRIC_L2SQ, cprec, 0, pv, probes));
+    if (!tc) {
+        VA_REQUIRE(nq <= 65535, "numQueries %lld exceeds 65535 per IVF call for k > 42", (long long)nq);
+        const size_t lb = (size_t)m * k;
+        VA_TRY(scratch(ctx, ivf, pb + lb * 8 + 256, pb, &ws));  // the probes move along
+        probes = (uint32_t*)ws;
+        float* cv = (float*)((uint8_t*)ws + pb);
+        uint32_t* ci = (uint32_t*)(cv + lb);
+        const size_t smem = (size_t)ivf->dim * 4;
+        if (smem > 48 * 1024)
+            VA_CUDA_TRY(cudaFuncSetAttribute(k_ivf_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        dim3 grid((unsigned)nprobe, (unsigned)nq);
+        k_ivf_scan<<<grid, LS_THREADS, smem, ctx->stream>>>(queries, nq, ivf->dim, probes, nprobe, ivf->rows,
+                                                           ivf->ids, ivf->offsets, k, cv, ci);
+        VA_TRY(va_check_launch("k_ivf_scan"));
+        return va_merge_lists_internal(ctx, cv, ci, nprobe, nq * k, k, nq, k, VA_SELECT_MIN, out_vals, out_ids);
+    }
+    // Pairs per (list, probe rank), read back: the query tiles are laid out on the host.
+    const int64_t nls = (int64_t)nlist * nprobe;
+    VA_CUDA_TRY(cudaMemsetAsync(cnt, 0, (size_t)nls * 4, ctx->stream));
+    k_probe_hist<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, cnt);
+    VA_TRY(va_check_launch("k_probe_hist"));
+    std::vector<int> h_cnt((size_t)nls);
+    VA_CUDA_TRY(cudaMemcpyAsync(h_cnt.data(), cnt, (size_t)nls * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_synchronize(ctx));
+    // A list's pairs in probe-rank order, cut into query tiles of 128. Tiles run by the rank of
+    // their first pair, then longest list first: the first rounds of the persistent grid scan
+    // every query's nearest lists, whose candidates set the per-query bounds that prune the
+    // farther lists' tiles.
+    std::vector<int> base((size_t)nls), lt0((size_t)nlist, 0);
+    struct TileKey {
+        int rank;
+        int64_t rows;
+        int list, j;
+    };
+    std::vector<TileKey> keys;
+    for (int L = 0; L < nlist; ++L) {
+        int acc = 0;
+        for (int r = 0; r < nprobe; ++r) {
+            base[(size_t)L * nprobe + r] = acc;
+            acc += h_cnt[(size_t)L * nprobe + r];
+        }
+        lt0[(size_t)L] = (int)keys.size();
+        const int64_t rows = ivf->h_offsets[(size_t)L + 1] - ivf->h_offsets[(size_t)L];
+        int r = 0;
+        for (int j = 0; j * 128 < acc; ++j) {
+            while (r + 1 < nprobe && base[(size_t)L * nprobe + r + 1] <= j * 128) ++r;
+            keys.push_back({r, rows, L, j});
+        }
+    }
+    const int n_qtiles = (int)keys.size();
+    std::vector<int> ord((size_t)n_qtiles);
+    for (int i = 0; i < n_qtiles; ++i) ord[(size_t)i] = i;
+    std::stable_sort(ord.begin(), ord.end(), [&](int x, int y) {
+        const TileKey &a = keys[(size_t)x], &b = keys[(size_t)y];
+        return a.rank != b.rank ? a.rank < b.rank : a.rows > b.rows;
+    });
+    std::vector<int> tile_list((size_t)n_qtiles), tile_of((size_t)n_qtiles);
+    for (int t = 0; t < n_qtiles; ++t) {
+        const TileKey& kt = keys[(size_t)ord[(size_t)t]];
+        tile_list[(size_t)t] = kt.list;
+        tile_of[(size_t)(lt0[(size_t)kt.list] + kt.j)] = t;
+    }
+    const int64_t G = (int64_t)n_qtiles * 128;
+    // Scratch layout after the probes and counts.
+    size_t off = head;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += round_up((int64_t)bytes, 256);
+        return o;
+    };
+    const size_t o_base = take((size_t)nls * 4), o_cur = take((size_t)nls * 4), o_lt0 = take((size_t)nlist * 4),
+                 o_tof = take((size_t)n_qtiles * 4), o_tiles = take((size_t)n_qtiles * 4),
+                 o_gmap = take((size_t)G * 4), o_ginv = take((size_t)m * 8), o_qop = take((size_t)G * ivf->dpad * 2),
+                 o_pk = take((size_t)G * kp * 4), o_pi = take((size_t)G * kp * 4), o_thr = take((size_t)G * 4);
+    VA_TRY(scratch(ctx, ivf, off, pb, &ws));  // the probes move along
+    uint8_t* sb = (uint8_t*)ws;
+    probes = (uint32_t*)sb;
+    int* d_base = (int*)(sb + o_base);
+    int* cursor = (int*)(sb + o_cur);
+    int* d_lt0 = (int*)(sb + o_lt0);
+    int* d_tof = (int*)(sb + o_tof);
+    int* d_tiles = (int*)(sb + o_tiles);
+    int* gmap = (int*)(sb + o_gmap);
+    int64_t* ginv = (int64_t*)(sb + o_ginv);
+    uint16_t* qop = (uint16_t*)(sb + o_qop);
+    float* pk = (float*)(sb + o_pk);
+    uint32_t* pi = (uint32_t*)(sb + o_pi);
+    uint32_t* gthr = (uint32_t*)(sb + o_thr);
+    VA_CUDA_TRY(cudaMemcpyAsync(d_base, base.data(), (size_t)nls * 4, cudaMemcpyHostToDevice, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(d_lt0, lt0.data(), (size_t)nlist * 4, cudaMemcpyHostToDevice, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(d_tof, tile_of.data(), (size_t)n_qtiles * 4, cudaMemcpyHostToDevice, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(d_tiles, tile_list.data(), (size_t)n_qtiles * 4, cudaMemcpyHostToDevice, ctx->stream));
+    VA_CUDA_TRY(cudaMemsetAsync(cursor, 0, (size_t)nls * 4, ctx->stream));
+    VA_CUDA_TRY(cudaMemsetAsync(gmap, 0xFF, (size_t)G * 4, ctx->stream));
+    k_probe_scatter<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, d_base, cursor, d_lt0, d_tof, gmap, ginv);
+    VA_TRY(va_check_launch("k_probe_scatter"));
+    k_rows_bf16<<<grid_for(G * ivf->dpad), 256, 0, ctx->stream>>>(queries, G, ivf->dim, ivf->dpad, gmap, nprobe, qop);
+    VA_TRY(va_check_launch("k_rows_bf16"));
+    TcFilterArgs a = {};
+    a.q_op = qop;
+    a.x_op = ivf->op;
+    a.elem_bytes = 2;
+    a.dpad = ivf->dpad;
+    a.n_rows = ivf->n;
+    a.row_bias = ivf->bias;
+    a.alpha = -2.f;
+    a.row_qn = nullptr;
+    a.part_keys = pk;
+    a.part_ids = pi;
+    a.gthr = gthr;
+    a.sync_cnt = nullptr;
+    a.sync_words = 0;
+    a.limit_ms = 2000u;
+    VA_TRY(va_tc_filter_lists(ctx, a, n_qtiles, d_tiles, ivf->offsets, gmap, nprobe, kp));
+    k_ivf_merge_rerank<<<(unsigned)nq, MR_THREADS, 0, ctx->stream>>>(queries, ivf->dim, ginv, nprobe, pk, pi, kp, pool,
+                                                                    k, ivf->rows, ivf->ids, out_vals, out_ids);
+    return va_check_launch("k_ivf_merge_rerank");
+}
+
+int va_ivf_search_host(va_context* ctx, const va_ivf* ivf, const float* queries_host, int64_t nq, int k, int nprobe,
+                       float* out_vals_host, uint32_t* out_ids_host) {
+    VA_REQUIRE(ctx && ivf && queries_host && out_vals_host && out_ids_host, "all pointers must be non-NULL");
+    VA_REQUIRE(nq > 0 && k > 0, "numQueries and k must be positive");
+    VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    const size_t qb = (size_t)nq * ivf->dim * 4, rb = (size_t)nq * k * 4;
+    void* io;
+    VA_TRY(va_io_buffer(ctx, round_up((int64_t)qb, 256) + 2 * round_up((int64_t)rb, 256), &io));
+    float* dq = (float*)io;
+    float* dv = (float*)((uint8_t*)io + round_up((int64_t)qb, 256));
+    uint32_t* di = (uint32_t*)((uint8_t*)dv + round_up((int64_t)rb, 256));
+    VA_CUDA_TRY(cudaMemcpyAsync(dq, queries_host, qb, cudaMemcpyHostToDevice, ctx->stream));
+    VA_TRY(va_ivf_search(ctx, ivf, dq, nq, k, nprobe, dv, di));
+    VA_CUDA_TRY(cudaMemcpyAsync(out_vals_host, dv, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(out_ids_host, di, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    return va_synchronize(ctx);
 }
 
 }  // extern "C"

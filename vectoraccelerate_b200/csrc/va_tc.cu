@@ -422,6 +422,16 @@ struct Work {
     // One slot at a high rank is available after the first item's first tiles; many slots at a
     // low rank are tighter once items of every split class have run.
     BoundLevels lv;
+    // List mode (single-CTA kernel only; null in a flat search): item i is query tile i, whose
+    // 128 queries are matched against list tile_list[i] alone, rows [list_off[L], list_off[L+1])
+    // of the operand. No row splits and no pacing.
+    const int* tile_list;
+    const int64_t* list_off;
+    // List mode: query tile row r holds (query, probe) pair row_pair[r] (-1: padding), of query
+    // row_pair[r] / pair_div. The bound slots are per query, shared by all of its probes' items
+    // (any item's KP-th key bounds the query's pool); padding rows neither read nor publish.
+    const int* row_pair;
+    int pair_div;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -456,6 +466,25 @@ __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int
     qt = item - s * w.n_qtiles;
     t0 = (int)(((int64_t)w.n_tiles * s) / w.splits);
     t1 = (int)(((int64_t)w.n_tiles * (s + 1)) / w.splits);
+}
+
+// An item's query tile, its row tiles [t0, t1) counted from row `rb`, and the end of its rows
+// (rows at or past `re` never pass). Flat search: rb = 0, re = n_rows.
+__device__ __forceinline__ void item_rows(const Work& w, int item, int& qt, int& t0, int& t1, int64_t& rb,
+                                          uint32_t& re) {
+    if (w.tile_list) {
+        qt = item;
+        const int L = w.tile_list[item];
+        rb = w.list_off[L];
+        const int64_t e = w.list_off[L + 1];
+        re = (uint32_t)e;
+        t0 = 0;
+        t1 = (int)((e - rb + BN - 1) / BN);
+    } else {
+        item_range(w, item, qt, t0, t1);
+        rb = 0;
+        re = (uint32_t)w.n_rows;
+    }
 }
 
 template <int ELEM, int KP>
@@ -519,11 +548,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool pace = true;
             for (int item = blockIdx.x; item < n_items && !*s_abort; item += gridDim.x, ++round) {
                 int qt, t0, t1;
-                item_range(w, item, qt, t0, t1);
+                int64_t rb;
+                uint32_t re;
+                item_rows(w, item, qt, t0, t1, rb, re);
                 int next_slot = 0;
                 for (int t = t0; t < t1; ++t) {
                     const int j = t - t0;
-                    if (j % w.chunk_tiles == 0) {
+                    if (w.sync_cnt && j % w.chunk_tiles == 0) {
                         const int g = round * w.cpr + j / w.chunk_tiles;
                         if (pace && g >= w.lag) {
                             const int gr = (g - w.lag) / w.cpr;
@@ -540,11 +571,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         mbar_expect_tx(&full[s], STAGE_BYTES);
                         const int kc = kb * (BKB / ELEM);
                         tma_load_2d(sA + (size_t)s * A_BYTES, &tmap_q, &full[s], kc, qt * BM);
-                        tma_load_2d(sB + (size_t)s * B_BYTES, &tmap_x, &full[s], kc, t * BN);
+                        tma_load_2d(sB + (size_t)s * B_BYTES, &tmap_x, &full[s], kc, (int)(rb + (int64_t)t * BN));
                     }
                 }
                 // A shorter item still arrives at every slot of its round.
-                for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
+                if (w.sync_cnt)
+                    for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
             }
         producer_done:;
         }
@@ -554,7 +586,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t it = 0, tile = 0;
             for (int item = blockIdx.x; item < n_items && !*s_abort; item += gridDim.x) {
                 int qt, t0, t1;
-                item_range(w, item, qt, t0, t1);
+                int64_t rb;
+                uint32_t re;
+                item_rows(w, item, qt, t0, t1, rb, re);
                 for (int t = t0; t < t1; ++t, ++tile) {
                     const uint32_t buf = tile & 1u;
                     const uint32_t tph = (tile >> 1) & 1u;
@@ -591,8 +625,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t tile = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             int qt, t0, t1;
-            item_range(w, item, qt, t0, t1);
+            int64_t rb;
+            uint32_t re;
+            item_rows(w, item, qt, t0, t1, rb, re);
             const int64_t q = (int64_t)qt * BM + row;
+            uint32_t* gq = gthr + q;
+            if (w.row_pair) {
+                const int pr = w.row_pair[q];
+                gq = pr >= 0 ? gthr + pr / w.pair_div : nullptr;
+            }
             // Reset this warp's 32 row lists (row-contiguous, KP entries each; coalesced).
             for (int e = lane; e < 32 * list_stride<KP>(); e += 32) {
                 l_key[quarter * 32 * list_stride<KP>() + e] = INFINITY;
@@ -600,24 +641,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             __syncwarp();
             const int qn = row_qn ? row_qn[q] : 0;
-            const uint32_t n_rows32 = (uint32_t)w.n_rows;
+            const uint32_t n_rows32 = re;
             float thr_own = INFINITY;
-            float thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
+            // Padding rows of a list-mode tile insert nothing (their lists are never read).
+            float thr_g = gq ? load_bound(gq, w.nq_pad, w.lv) : -INFINITY;
             float thr = thr_g;
             // The tile's 256 row biases (|x|^2 for L2, 0 otherwise; +inf past the last row): lane j
             // holds columns j + 32r, r < 8; the next tile's are prefetched while this one runs.
             float bias[8], nbias[8];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + (int64_t)t0 * BN + lane + 32 * r);
+            for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + rb + (int64_t)t0 * BN + lane + 32 * r);
             const int split = item / w.n_qtiles;
             const float* const row_keys = l_key + (size_t)row * list_stride<KP>();
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 3) == 3) {
-                    publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
-                    thr_g = load_bound(gthr + q, w.nq_pad, w.lv);
+                    if (gq) {
+                        publish_bound(gq, w.nq_pad, w.lv, split, row_keys);
+                        thr_g = load_bound(gq, w.nq_pad, w.lv);
+                    }
                     thr = fminf(thr_own, thr_g);
                 }
-                const int64_t col0 = (int64_t)t * BN;
+                const int64_t col0 = rb + (int64_t)t * BN;
                 if (t + 1 < t1) {
 #pragma unroll
                     for (int r = 0; r < 8; ++r) nbias[r] = __ldg(row_bias + col0 + BN + lane + 32 * r);
@@ -660,7 +704,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             {
                 // Publish this item's final rank keys as bounds.
                 const int s = split;
-                publish_bound(gthr + q, w.nq_pad, w.lv, split, row_keys);
+                if (gq) publish_bound(gq, w.nq_pad, w.lv, split, row_keys);
                 // The warp's 32 lists are contiguous in shared memory and in the output
                 // ([split][query][KP]): copy them with coalesced stores.
                 const int64_t out0 = ((int64_t)s * w.nq_pad + (int64_t)qt * BM + quarter * 32) * KP;
@@ -1046,7 +1090,8 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
     int total_slots = 0;
     for (int l = 0; l < w.lv.n; ++l) total_slots += w.lv.slots[l];
     VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)total_slots * w.nq_pad * sizeof(uint32_t), ctx->stream));
-    VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
+    if (w.sync_cnt)
+        VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
     // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
     // The pair kernel also runs as clusters of two CTAs.
     cudaLaunchConfig_t cfg = {};
@@ -1202,6 +1247,10 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.cpr = p.cpr;
     w.lag = p.lag;
     w.sync_cnt = a.sync_cnt;
+    w.tile_list = nullptr;
+    w.list_off = nullptr;
+    w.row_pair = nullptr;
+    w.pair_div = 1;
     w.lv = a.levels.n > 0 ? a.levels : one_level(p.kp);
     for (int l = 0; l < w.lv.n; ++l)
         if (w.lv.rank[l] < 1 || w.lv.rank[l] > p.kp || w.lv.slots[l] < 1)
@@ -1225,4 +1274,42 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
         if (p.kp == 128) return launch_filter<4, 128>(ctx, a, stages, smem, mq, mx, w, p.grid, p.pair);
     }
     return va_set_error(VA_ERR_UNSUPPORTED, "candidate pool %d not supported by the tensor-core filter", p.kp);
+}
+
+// List mode: query tile i (128 gathered queries) against the rows of list tile_list[i] only. One
+// item per query tile (no row splits, no pacing), at most one CTA per SM, the single-CTA kernel.
+// Lists go out as [n_qtiles * 128][kp]. The bound is per query (row_pair[r] / pair_div for query
+// tile row r; -1 = padding): a.gthr needs max(queries, n_qtiles * 128) words.
+int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, const int* tile_list,
+                       const int64_t* list_off, const int* row_pair, int pair_div, int kp) {
+    if (n_qtiles <= 0) return VA_OK;
+    VA_REQUIRE(kp == 32 || kp == 64 || kp == 128, "list length %d not supported", kp);
+    VA_REQUIRE(a.elem_bytes == 2, "list mode takes bf16 operands");
+    CUtensorMap mq, mx;
+    const int64_t nq_pad = (int64_t)n_qtiles * BM;
+    VA_TRY(make_tmap(&mq, a.q_op, nq_pad, a.dpad, 2, BM));
+    VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, 2, BN));
+    Work w = {};
+    w.n_qtiles = n_qtiles;
+    w.splits = 1;
+    w.n_tiles = 0;
+    w.k_blocks = (int)((a.dpad * 2 + BKB - 1) / BKB);
+    w.n_rows = a.n_rows;
+    w.nq_pad = nq_pad;
+    w.chunk_tiles = 1;
+    w.cpr = 1;
+    w.lag = 0;
+    w.sync_cnt = nullptr;
+    w.lv = one_level(kp);
+    w.tile_list = tile_list;
+    w.list_off = list_off;
+    w.row_pair = row_pair;
+    w.pair_div = pair_div;
+    const int stages = va_tc_stages(kp, false);
+    if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "list length %d too large for shared memory", kp);
+    const size_t smem = smem_bytes(kp, stages, false);
+    const int grid = std::min(n_qtiles, ctx->sm_count);
+    if (kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, grid, false);
+    if (kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, grid, false);
+    return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, grid, false);
 }

@@ -60,3 +60,9 @@ int va_tc_plan_pool(va_context* ctx, int64_t nq, int64_t n_rows, int pool, TcPla
 int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
 int va_tc_stages(int kp, bool pair);
 bool va_tc_use_pair();
+// List mode (IVF list scan): query tile i against the rows [list_off[L], list_off[L+1]) of list
+// L = tile_list[i] (device arrays); lists out as [n_qtiles * 128][kp]; a.sync_cnt unused. Row r
+// of the query tiles is (query, probe) pair row_pair[r] (-1: padding) of query row_pair[r] /
+// pair_div; the shared bound is per query.
+int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, const int* tile_list,
+                       const int64_t* list_off, const int* row_pair, int pair_div, int kp);

@@ -219,9 +219,16 @@ class IVFSearchPipeline:
         if q.shape[1] != structure.dimension:
             raise InvalidInput(f"query dimension {q.shape[1]} != index dimension {structure.dimension}")
         nprobe = min(self.configuration.nprobe, structure.num_centroids)
-        ctx = self.context
-        dq = ctx.get_buffer_for(q)
-        ov = ctx.get_buffer(4 * q.shape[0] * k, np.float32, (q.shape[0], k))
-        oi = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
-        _ffi.call("va_ivf_search", ctx.handle, structure.handle, dq.ptr, q.shape[0], k, nprobe, ov.ptr, oi.ptr)
-        return IVFSearchResult(indices=oi.download(), distances=ov.download())
+        ov = np.empty((q.shape[0], k), np.float32)
+        oi = np.empty((q.shape[0], k), np.uint32)
+        _ffi.call("va_ivf_search_host", self.context.handle, structure.handle, q.ctypes.data_as(_vp), q.shape[0], k,
+                  nprobe, ov.ctypes.data_as(_vp), oi.ctypes.data_as(_vp))
+        return IVFSearchResult(indices=oi, distances=ov)
+
+    def search_device(self, queries_ptr: int, nq: int, structure: IVFGPUIndexStructure, k: int, out_values_ptr: int,
+                      out_indices_ptr: int) -> None:
+        """Device-resident form: queries [nq x dimension] fp32 and outputs [nq x k] in device
+        memory (stream-ordered on the context's stream)."""
+        nprobe = min(self.configuration.nprobe, structure.num_centroids)
+        _ffi.call("va_ivf_search", self.context.handle, structure.handle, queries_ptr, nq, k, nprobe, out_values_ptr,
+                  out_indices_ptr)
