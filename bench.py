@@ -56,10 +56,17 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=1_000_000, help="database rows of the CPU sample")
     p.add_argument("--no-clocks", action="store_true")
-    p.add_argument("--config", choices=["headline"] + sorted(CONFIGS), default="headline",
-                   help="headline (the default bench line) or one of the other BASELINE configurations")
+    p.add_argument("--config", choices=["headline"] + sorted(CONFIGS) + ["ivf"], default="headline",
+                   help="headline (the default bench line), one of the other BASELINE configurations, or ivf "
+                        "(the IVF search, not a BASELINE configuration)")
+    p.add_argument("--nlist", type=int, default=1024, help="ivf: inverted lists")
+    p.add_argument("--nprobe", type=int, default=32, help="ivf: lists probed per query")
     a = p.parse_args()
-    if a.config != "headline":
+    if a.config == "ivf":
+        for key, v in (("n", 1_000_000), ("dim", 128), ("nq", 10_000), ("k", 10)):
+            if getattr(a, key) == p.get_default(key):
+                setattr(a, key, v)
+    elif a.config != "headline":
         # the other configurations carry their own sizes unless given explicitly
         c = CONFIGS[a.config]
         for key in ("n", "dim", "nq", "k"):
@@ -620,10 +627,104 @@ def run_config(a):
         dist.destroy_process_group()
 
 
+def run_ivf(a):
+    """IVF search (not a BASELINE configuration): k-means lists over a mixture on one GPU, then
+    K timed searches of the same query batch, device-resident (`value`) and through the host-buffer
+    entry (`e2e`); recall@k against the exact flat search. Further ranks exit (replicas only)."""
+    import torch
+
+    import vectoraccelerate_b200 as va
+    from vectoraccelerate_b200 import _ffi
+
+    rank, world, local = env_rank()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
+    n, dim, nq, k, nlist, nprobe = a.n, a.dim, a.nq, a.k, a.nlist, a.nprobe
+    x = torch.empty((n, dim), dtype=torch.float32, device="cuda")
+    q = torch.empty((nq, dim), dtype=torch.float32, device="cuda")
+    _ffi.call("va_gen_mixture", ctx.handle, x.data_ptr(), n, dim, 7, 0, 256, ctypes.c_float(0.5), 0)
+    _ffi.call("va_gen_mixture", ctx.handle, q.data_ptr(), nq, dim, 7, QUERY_ROW0, 256, ctypes.c_float(0.5), 0)
+    cent = torch.empty((nlist, dim), dtype=torch.float32, device="cuda")
+    iters = ctypes.c_int(0)
+    t0 = time.perf_counter()
+    _ffi.call("va_ivf_train", ctx.handle, x.data_ptr(), n, dim, nlist, 20, ctypes.c_float(1e-3), 42, 0,
+              cent.data_ptr(), ctypes.byref(iters))
+    ctx.synchronize()
+    t_train = time.perf_counter() - t0
+    h = ctypes.c_void_p()
+    _ffi.call("va_ivf_create", ctx.handle, x.data_ptr(), n, dim, cent.data_ptr(), nlist, 0, ctypes.byref(h))
+    ctx.synchronize()
+    ov = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    oi = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    hq = q.cpu().pin_memory()
+    hv = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    hi = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+
+    def step():
+        _ffi.call("va_ivf_search", ctx.handle, h.value, q.data_ptr(), nq, k, nprobe, ov.data_ptr(), oi.data_ptr())
+
+    for _ in range(a.warmup):
+        step()
+    ctx.synchronize()
+    clocks = ClockSampler(str(local), enabled=not a.no_clocks)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(a.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / a.steps
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        _ffi.call("va_ivf_search_host", ctx.handle, h.value, hq.data_ptr(), nq, k, nprobe, hv.data_ptr(),
+                  hi.data_ptr())
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / a.steps
+    sizes = np.zeros(nlist, np.int64)
+    _ffi.call("va_ivf_list_sizes", h.value, sizes.ctypes.data_as(ctypes.c_void_p))
+    # recall@k against the exact flat search of the same rows
+    db = va.Database(ctx, None, device_ptr=x.data_ptr(), n=n, dim=dim)
+    ev_, ei_ = torch.empty_like(ov), torch.empty_like(oi)
+    _ffi.call("va_knn_search", ctx.handle, db.handle, q.data_ptr(), nq, k, _ffi.METRIC_L2SQ, _ffi.PREC_AUTO, 0,
+              ev_.data_ptr(), ei_.data_ptr())
+    ctx.synchronize()
+    got, ref = oi.cpu().numpy(), ei_.cpu().numpy()
+    recall = float(np.mean([len(set(got[i]) & set(ref[i])) / k for i in range(nq)]))
+    db.close()
+    _ffi.call("va_ivf_destroy", h.value)
+    line = {
+        "metric": f"queries/sec, IVF search (nlist {nlist}, nprobe {nprobe}); not a BASELINE configuration",
+        "value": nq / (ms * 1e-3), "unit": "queries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+        "dtype": "bf16 list scan + f64 exact rerank (fp32 coarse quantizer)",
+        "data": "synthetic: mixture of 256 centroids sigma 0.5 (TestRNG restatement on the device)",
+        "config": {"workload": f"IVF k-NN: N={n:,} x d={dim} fp32, k-means {nlist} lists ({iters.value} iterations, "
+                               f"{t_train:.2f} s), Q={nq:,}, k={k}, nprobe={nprobe}",
+                   "config": "ivf", "N": n, "d": dim, "Q": nq, "k": k, "nlist": nlist, "nprobe": nprobe,
+                   f"recall@{k}_vs_exact": recall,
+                   "list_rows_min_mean_max": [int(sizes.min()), float(sizes.mean()), int(sizes.max())],
+                   "l2_policy": "rows (512 MB) larger than L2, no flush"},
+        "e2e": {"value": nq / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
+                "d2h_bytes_per_step": nq * k * 8},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
-    if a.impl == "reference":
+    if a.impl == "reference" and a.config == "ivf":
+        print(json.dumps({"impl": "reference", "unavailable": "no reference arm for the ivf configuration "
+                          "(not a BASELINE configuration)"}), flush=True)
+    elif a.impl == "reference":
         run_reference(a)
+    elif a.config == "ivf":
+        run_ivf(a)
     elif a.config != "headline":
         run_config(a)
     else:

@@ -428,10 +428,11 @@ struct Work {
     const int* tile_list;
     const int64_t* list_off;
     // List mode: query tile row r holds (query, probe) pair row_pair[r] (-1: padding), of query
-    // row_pair[r] / pair_div. The bound slots are per query, shared by all of its probes' items
+    // row_pair[r] / pair_div. The bound slot is per query, shared by all of its probes' items
     // (any item's KP-th key bounds the query's pool); padding rows neither read nor publish.
     const int* row_pair;
     int pair_div;
+    int item_base;  // list mode: item i is query tile item_base + i
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -473,8 +474,8 @@ __device__ __forceinline__ void item_range(const Work& w, int item, int& qt, int
 __device__ __forceinline__ void item_rows(const Work& w, int item, int& qt, int& t0, int& t1, int64_t& rb,
                                           uint32_t& re) {
     if (w.tile_list) {
-        qt = item;
-        const int L = w.tile_list[item];
+        qt = w.item_base + item;
+        const int L = w.tile_list[qt];
         rb = w.list_off[L];
         const int64_t e = w.list_off[L + 1];
         re = (uint32_t)e;
@@ -634,6 +635,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const int pr = w.row_pair[q];
                 gq = pr >= 0 ? gthr + pr / w.pair_div : nullptr;
             }
+            const int split = item / w.n_qtiles;
             // Reset this warp's 32 row lists (row-contiguous, KP entries each; coalesced).
             for (int e = lane; e < 32 * list_stride<KP>(); e += 32) {
                 l_key[quarter * 32 * list_stride<KP>() + e] = INFINITY;
@@ -651,7 +653,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float bias[8], nbias[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r) bias[r] = __ldg(row_bias + rb + (int64_t)t0 * BN + lane + 32 * r);
-            const int split = item / w.n_qtiles;
             const float* const row_keys = l_key + (size_t)row * list_stride<KP>();
             for (int t = t0; t < t1; ++t, ++tile) {
                 if (((t - t0) & 3) == 3) {
@@ -1084,12 +1085,13 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_ele
 
 template <int ELEM, int KP>
 int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t smem, const CUtensorMap& mq,
-                  const CUtensorMap& mx, const Work& w, int grid, bool pair) {
+                  const CUtensorMap& mx, const Work& w, int grid, bool pair, bool reset_bounds = true) {
     auto kern = pair ? k_tc_filter_pair<ELEM, KP> : k_tc_filter<ELEM, KP>;
     VA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int total_slots = 0;
     for (int l = 0; l < w.lv.n; ++l) total_slots += w.lv.slots[l];
-    VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)total_slots * w.nq_pad * sizeof(uint32_t), ctx->stream));
+    if (reset_bounds)
+        VA_CUDA_TRY(cudaMemsetAsync(a.gthr, 0xFF, (size_t)total_slots * w.nq_pad * sizeof(uint32_t), ctx->stream));
     if (w.sync_cnt)
         VA_CUDA_TRY(cudaMemsetAsync(w.sync_cnt, 0, (size_t)a.sync_words * sizeof(uint32_t), ctx->stream));
     // Cooperative launch: the CTAs pace each other, so all of them must be resident at once.
@@ -1251,6 +1253,7 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.list_off = nullptr;
     w.row_pair = nullptr;
     w.pair_div = 1;
+    w.item_base = 0;
     w.lv = a.levels.n > 0 ? a.levels : one_level(p.kp);
     for (int l = 0; l < w.lv.n; ++l)
         if (w.lv.rank[l] < 1 || w.lv.rank[l] > p.kp || w.lv.slots[l] < 1)
@@ -1278,19 +1281,24 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
 
 // List mode: query tile i (128 gathered queries) against the rows of list tile_list[i] only. One
 // item per query tile (no row splits, no pacing), at most one CTA per SM, the single-CTA kernel.
-// Lists go out as [n_qtiles * 128][kp]. The bound is per query (row_pair[r] / pair_div for query
-// tile row r; -1 = padding): a.gthr needs max(queries, n_qtiles * 128) words.
-int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, const int* tile_list,
-                       const int64_t* list_off, const int* row_pair, int pair_div, int kp) {
-    if (n_qtiles <= 0) return VA_OK;
+// This launch runs tiles [tile0, tile0 + tiles) of n_qtiles; lists go out as [n_qtiles * 128][kp].
+// The bound is per query (row_pair[r] / pair_div for query tile row r; -1 = padding), one slot at
+// rank kp: a.gthr needs n_qtiles * 128 words, reset (to "none") when reset_bounds, else kept from
+// the previous launch.
+int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, int tile0, int tiles,
+                       const int* tile_list, const int64_t* list_off, const int* row_pair, int pair_div, int kp,
+                       bool reset_bounds) {
+    if (tiles <= 0) return VA_OK;
     VA_REQUIRE(kp == 32 || kp == 64 || kp == 128, "list length %d not supported", kp);
     VA_REQUIRE(a.elem_bytes == 2, "list mode takes bf16 operands");
+    VA_REQUIRE(tile0 >= 0 && tile0 + tiles <= n_qtiles, "tile range [%d, %d) outside %d tiles", tile0, tile0 + tiles,
+               n_qtiles);
     CUtensorMap mq, mx;
     const int64_t nq_pad = (int64_t)n_qtiles * BM;
     VA_TRY(make_tmap(&mq, a.q_op, nq_pad, a.dpad, 2, BM));
     VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, 2, BN));
     Work w = {};
-    w.n_qtiles = n_qtiles;
+    w.n_qtiles = tiles;
     w.splits = 1;
     w.n_tiles = 0;
     w.k_blocks = (int)((a.dpad * 2 + BKB - 1) / BKB);
@@ -1305,11 +1313,12 @@ int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, con
     w.list_off = list_off;
     w.row_pair = row_pair;
     w.pair_div = pair_div;
+    w.item_base = tile0;
     const int stages = va_tc_stages(kp, false);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "list length %d too large for shared memory", kp);
     const size_t smem = smem_bytes(kp, stages, false);
-    const int grid = std::min(n_qtiles, ctx->sm_count);
-    if (kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, grid, false);
-    if (kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, grid, false);
-    return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, grid, false);
+    const int grid = std::min(tiles, ctx->sm_count);
+    if (kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
+    if (kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
+    return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
 }

@@ -61,8 +61,10 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p);
 int va_tc_stages(int kp, bool pair);
 bool va_tc_use_pair();
 // List mode (IVF list scan): query tile i against the rows [list_off[L], list_off[L+1]) of list
-// L = tile_list[i] (device arrays); lists out as [n_qtiles * 128][kp]; a.sync_cnt unused. Row r
-// of the query tiles is (query, probe) pair row_pair[r] (-1: padding) of query row_pair[r] /
-// pair_div; the shared bound is per query.
-int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, const int* tile_list,
-                       const int64_t* list_off, const int* row_pair, int pair_div, int kp);
+// L = tile_list[i] (device arrays); this launch runs tiles [tile0, tile0 + tiles) of n_qtiles;
+// lists out as [n_qtiles * 128][kp]; a.sync_cnt unused. Row r of the query tiles is (query,
+// probe) pair row_pair[r] (-1: padding) of query row_pair[r] / pair_div; the shared bound is per
+// query, reset before the launch when reset_bounds (else kept from the previous launch).
+int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, int tile0, int tiles,
+                       const int* tile_list, const int64_t* list_off, const int* row_pair, int pair_div, int kp,
+                       bool reset_bounds);
