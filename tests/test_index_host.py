@@ -76,3 +76,14 @@ def test_batch_search_shapes_and_errors():
     assert [r.count for r in out] == [3, 3]
     assert all(x.distance == pytest.approx(4.0) for x in out[0].results)
     assert _ffi.INVALID_ID == 0xFFFFFFFF
+
+
+def test_ivf_configuration_validation():
+    import vectoraccelerate_b200 as va
+    c = va.IndexConfiguration.ivf(8, nlist=4, nprobe=2)
+    assert c.is_ivf and c.routing_threshold == 10_000 and c.capacity == 100_000
+    assert not va.IndexConfiguration.flat(8).is_ivf
+    with pytest.raises(va.InvalidInput):
+        va.IndexConfiguration.ivf(8, nlist=4, nprobe=5)
+    with pytest.raises(va.InvalidInput):
+        va.IndexConfiguration.ivf(8, nlist=4, nprobe=2, metric="cosine")

@@ -14,6 +14,16 @@ Rows live in a resident device database created on the first search and then kep
 the device: inserts append to it (va_db_append, geometric growth) and compaction gathers its kept
 rows (va_db_compact), as GPUVectorStorage writes and compacts its buffer. A host copy of the rows
 serves ``vector(for:)`` and the exhaustive tail of a filtered search.
+
+IVF indexes (``IndexConfiguration.ivf``, IndexConfiguration.swift:274-290,347-370) follow the
+reference's routing: until trained, and while fewer vectors than ``routing_threshold`` are live,
+searches are flat; ``train()`` (:396-446) runs k-means over the live vectors (25 iterations,
+movement threshold 1e-3, as IVFStructure.swift:218-222) and inserts train automatically once
+``min_training_vectors`` (default max(10 nlist, 1000), IVFStructure.swift:187) are staged
+(:529-545). A trained index searches its lists (searchIVF / searchIVFBatch, :1378-1470): the
+lists are rebuilt on the device from the resident rows after any change, slots are the ids, and
+deleted slots are skipped after an over-fetch of k + deleted (at most 128); a filtered single-query
+search over-fetches 3k and filters (:1397-1420). k above 128 is served by the flat search.
 """
 
 from __future__ import annotations
@@ -35,15 +45,32 @@ VectorMetadata = dict  # [String: String] (AcceleratedVectorIndex.swift:22)
 
 @dataclass(frozen=True)
 class IndexConfiguration:
-    """IndexConfiguration.flat(dimension:metric:capacity:) (Index/Types/IndexConfiguration.swift:330-345)."""
+    """IndexConfiguration (Index/Types/IndexConfiguration.swift:230-370): ``flat(...)`` and
+    ``ivf(...)``. index_type is ("flat",) or ("ivf", nlist, nprobe, min_training_vectors)."""
 
     dimension: int
     metric: str = "euclidean"
     capacity: int = 1024
+    index_type: tuple = ("flat",)
+    routing_threshold: int = 0
 
     @staticmethod
     def flat(dimension: int, metric: str = "euclidean", capacity: int = 1024) -> "IndexConfiguration":
         return IndexConfiguration(dimension, metric, capacity)
+
+    @staticmethod
+    def ivf(dimension: int, nlist: int, nprobe: int, metric: str = "euclidean", capacity: int = 100_000,
+            routing_threshold: int = 10_000, min_training_vectors: Optional[int] = None) -> "IndexConfiguration":
+        if nlist <= 0 or not 1 <= nprobe <= nlist:
+            raise VAIndexError(f"IVF needs nlist > 0 and 1 <= nprobe <= nlist, got {nlist} / {nprobe}")
+        if metric != "euclidean":
+            raise VAIndexError("the IVF index is euclidean (squared L2) only")
+        return IndexConfiguration(dimension, metric, capacity, ("ivf", nlist, nprobe, min_training_vectors),
+                                  routing_threshold)
+
+    @property
+    def is_ivf(self) -> bool:
+        return self.index_type[0] == "ivf"
 
 
 @dataclass(frozen=True)
@@ -91,6 +118,11 @@ class AcceleratedVectorIndex:
         self._metadata: dict[int, VectorMetadata] = {}
         self._next_handle = 0
         self._db: Database | None = None
+        # IVF state: trained centroids, the device lists (rebuilt after any change), auto-training
+        self._centroids: np.ndarray | None = None
+        self._ivf = None
+        self._ivf_dirty = True
+        self._auto_train = True
 
     # ------------------------------------------------------------------------- mutation
     def insert(self, vector, metadata: Optional[VectorMetadata] = None) -> VectorHandle:
@@ -118,6 +150,12 @@ class AcceleratedVectorIndex:
             handles.append(VectorHandle(h))
         if self._db is not None:
             self._db.append(v)
+        self._ivf_dirty = True
+        cfg = self.configuration
+        if cfg.is_ivf and self._centroids is None and self._auto_train:
+            min_train = cfg.index_type[3] or max(10 * cfg.index_type[1], 1000)
+            if self.count >= min_train:
+                self.train()
         return handles
 
     def remove(self, handle: VectorHandle) -> None:
@@ -126,6 +164,7 @@ class AcceleratedVectorIndex:
             raise VAIndexError(f"unknown handle {handle.value}")
         self._deleted[slot] = True
         self._metadata.pop(handle.value, None)
+        self._ivf_dirty = True
 
     def remove_batch(self, handles) -> int:
         """remove(_ handles:) (:800-832): removes the live ones, returns how many."""
@@ -147,6 +186,7 @@ class AcceleratedVectorIndex:
             else:
                 self._db.close()
                 self._db = None
+        self._ivf_dirty = True
         self._rows = np.ascontiguousarray(self._rows[keep])
         self._slot_handle = [h for h, k in zip(self._slot_handle, keep) if k]
         self._handle_slot = {h: s for s, h in enumerate(self._slot_handle)}
@@ -159,6 +199,67 @@ class AcceleratedVectorIndex:
             self._metadata.pop(handle.value, None)
         else:
             self._metadata[handle.value] = dict(metadata)
+
+    # ------------------------------------------------------------------------- IVF
+    @property
+    def is_ivf(self) -> bool:
+        return self.configuration.is_ivf
+
+    @property
+    def is_trained(self) -> bool:
+        """Always true for a flat index (:349-352)."""
+        return not self.is_ivf or self._centroids is not None
+
+    def set_auto_training(self, enabled: bool) -> None:
+        self._auto_train = bool(enabled)
+
+    def train(self) -> None:
+        """k-means over the live vectors (:396-446); a flat or trained index is left as is."""
+        from .ivf import KMeansConfiguration, KMeansPipeline
+        if not self.is_ivf or self._centroids is not None:
+            return
+        live = self._rows[~self._deleted]
+        if live.shape[0] == 0:
+            raise VAIndexError("Cannot train IVF index with no vectors")
+        nlist = self.configuration.index_type[1]
+        if live.shape[0] < nlist:
+            raise VAIndexError(f"IVF training needs at least nlist ({nlist}) vectors, got {live.shape[0]}")
+        cfg = KMeansConfiguration(num_clusters=nlist, dimension=self.configuration.dimension, max_iterations=25,
+                                  convergence_threshold=1e-3)
+        self._centroids = KMeansPipeline(self.context, cfg).fit(live).centroids
+        self._ivf_dirty = True
+
+    def _ivf_route(self, k: int) -> bool:
+        cfg = self.configuration
+        if not cfg.is_ivf or self._centroids is None or k > 128:
+            return False
+        return not (cfg.routing_threshold > 0 and self.count < cfg.routing_threshold)
+
+    def _ivf_structure(self):
+        import ctypes
+
+        from .ivf import IVFGPUIndexStructure
+        if self._ivf is None or self._ivf_dirty:
+            if self._ivf is not None:
+                self._ivf.close()
+                self._ivf = None
+            db = self._database()
+            dc = self.context.get_buffer_for(self._centroids)
+            h = ctypes.c_void_p()
+            nlist = self._centroids.shape[0]
+            _ffi.call("va_ivf_create", self.context.handle, db.rows_ptr(), self._rows.shape[0],
+                      self.configuration.dimension, dc.ptr, nlist, 0, ctypes.byref(h))
+            self._ivf = IVFGPUIndexStructure(self.context, h.value, nlist, self.configuration.dimension)
+            self._ivf_dirty = False
+        return self._ivf
+
+    def _ivf_fetch(self, q: np.ndarray, fetch_k: int):
+        from .ivf import IVFSearchConfiguration, IVFSearchPipeline
+        st = self._ivf_structure()
+        nlist, nprobe = self.configuration.index_type[1], self.configuration.index_type[2]
+        res = IVFSearchPipeline(self.context, IVFSearchConfiguration(nlist, nprobe, self.configuration.dimension)) \
+            .search(q, st, fetch_k)
+        return res.distances, res.indices
 
     # ------------------------------------------------------------------------- queries on handles
     @property
@@ -231,11 +332,16 @@ class AcceleratedVectorIndex:
         allocated = self._rows.shape[0]
         if allocated == 0 or self.count == 0:
             return [SearchResults([]) for _ in range(q.shape[0])]
-        if filter is not None:
-            return [self._search_filtered(q[r:r + 1], k, filter) for r in range(q.shape[0])]
         deleted = int(self._deleted.sum())
-        fetch_k = min(k + deleted, allocated)
-        vals, ids = self._fetch(q, fetch_k)
+        ivf = self._ivf_route(k)
+        if filter is not None:
+            if ivf and q.shape[0] == 1:
+                return [self._search_ivf_filtered(q, k, filter)]
+            return [self._search_filtered(q[r:r + 1], k, filter) for r in range(q.shape[0])]
+        if ivf:
+            vals, ids = self._ivf_fetch(q, min(k + deleted, 128))
+        else:
+            vals, ids = self._fetch(q, min(k + deleted, allocated))
         out = []
         for r in range(q.shape[0]):
             res = []
@@ -246,8 +352,24 @@ class AcceleratedVectorIndex:
                 res.append(IndexSearchResult(VectorHandle(self._slot_handle[i]), float(v)))
                 if len(res) == k:
                     break
-            out.append(SearchResults(res, candidates_searched=allocated))
+            out.append(SearchResults(res, candidates_searched=allocated, is_exhaustive=not ivf))
         return out
+
+    def _search_ivf_filtered(self, q: np.ndarray, k: int, filter: Filter) -> SearchResults:  # noqa: A002
+        """searchIVF with a filter (:1397-1420): over-fetch 3k (at most 128), skip deleted slots,
+        keep what passes the filter."""
+        vals, ids = self._ivf_fetch(q, min(3 * k, 128))
+        res = []
+        for i, v in zip(ids[0], vals[0]):
+            i = int(i)
+            if i == _ffi.INVALID_ID or self._deleted[i]:
+                continue
+            h = VectorHandle(self._slot_handle[i])
+            if filter(h, self._metadata.get(h.value)):
+                res.append(IndexSearchResult(h, float(v)))
+                if len(res) >= k:
+                    break
+        return SearchResults(res, candidates_searched=self.count, is_exhaustive=False)
 
     def _search_filtered(self, q: np.ndarray, k: int, filter: Filter) -> SearchResults:  # noqa: A002
         """searchFiltered (:1188-1265): fetch 2k, double until k results pass the filter or every
