@@ -61,6 +61,8 @@ def parse_args():
                         "(the IVF search, not a BASELINE configuration)")
     p.add_argument("--nlist", type=int, default=1024, help="ivf: inverted lists")
     p.add_argument("--nprobe", type=int, default=32, help="ivf: lists probed per query")
+    p.add_argument("--kmeans-iters", type=int, default=20, help="ivf: k-means iteration limit")
+    p.add_argument("--kmeans-tol", type=float, default=1e-3, help="ivf: k-means movement threshold")
     a = p.parse_args()
     if a.config == "ivf":
         for key, v in (("n", 1_000_000), ("dim", 128), ("nq", 10_000), ("k", 10)):
@@ -651,8 +653,8 @@ def run_ivf(a):
     cent = torch.empty((nlist, dim), dtype=torch.float32, device="cuda")
     iters = ctypes.c_int(0)
     t0 = time.perf_counter()
-    _ffi.call("va_ivf_train", ctx.handle, x.data_ptr(), n, dim, nlist, 20, ctypes.c_float(1e-3), 42, 0,
-              cent.data_ptr(), ctypes.byref(iters))
+    _ffi.call("va_ivf_train", ctx.handle, x.data_ptr(), n, dim, nlist, a.kmeans_iters, ctypes.c_float(a.kmeans_tol),
+              42, 0, cent.data_ptr(), ctypes.byref(iters))
     ctx.synchronize()
     t_train = time.perf_counter() - t0
     h = ctypes.c_void_p()

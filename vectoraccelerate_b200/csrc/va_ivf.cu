@@ -194,20 +194,23 @@ __global__ void k_row_norms(const float* __restrict__ x, int64_t n, int dim, int
     if (lane == 0) bias[r] = (float)s;
 }
 
-// cnt[L * nprobe + s] = pairs of probe rank s (the s-th nearest centroid) that fall on list L.
-__global__ void k_probe_hist(const uint32_t* __restrict__ probes, int64_t m, int nprobe, int* __restrict__ cnt) {
+// Probe-rank bucket of pair i: its rank (the rank-th nearest centroid), ranks >= nb - 1 together.
+__device__ __forceinline__ int rank_bucket(int64_t i, int nprobe, int nb) { return min((int)(i % nprobe), nb - 1); }
+
+// cnt[L * nb + b] = pairs of rank bucket b that fall on list L.
+__global__ void k_probe_hist(const uint32_t* __restrict__ probes, int64_t m, int nprobe, int nb, int* __restrict__ cnt) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
-        atomicAdd(cnt + (int64_t)probes[i] * nprobe + (int)(i % nprobe), 1);
+        atomicAdd(cnt + (int64_t)probes[i] * nb + rank_bucket(i, nprobe, nb), 1);
 }
 
 // Every (query, probe) pair takes a row of its list's query tiles, the list's pairs ordered by
-// probe rank: position p = base[L, s] + arrival within (L, s), in tile tile_of[lt0[L] + p / 128]
+// rank bucket: position p = base[L, b] + arrival within (L, b), in tile tile_of[lt0[L] + p / 128]
 // at row p % 128. gmap[g] = pair, ginv[pair] = g.
-__global__ void k_probe_scatter(const uint32_t* __restrict__ probes, int64_t m, int nprobe,
+__global__ void k_probe_scatter(const uint32_t* __restrict__ probes, int64_t m, int nprobe, int nb,
                                 const int* __restrict__ base, int* __restrict__ cursor, const int* __restrict__ lt0,
                                 const int* __restrict__ tile_of, int* __restrict__ gmap, int64_t* __restrict__ ginv) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t ls = (int64_t)probes[i] * nprobe + (int)(i % nprobe);
+        const int64_t ls = (int64_t)probes[i] * nb + rank_bucket(i, nprobe, nb);
         const int p = base[ls] + atomicAdd(cursor + ls, 1);
         const int64_t g = (int64_t)tile_of[lt0[probes[i]] + p / 128] * 128 + p % 128;
         gmap[g] = (int)i;
@@ -647,6 +650,10 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     va_ivf* ivf = const_cast<va_ivf*>(civf);  // only its search scratch changes
     const int64_t m = nq * nprobe;
+    VA_REQUIRE(m < ((int64_t)1 << 31) - 65536, "numQueries x nprobe (%lld) must stay below 2^31 per IVF call",
+               (long long)m);
+    // Pairs are ordered by probe rank in up to 8 buckets (ranks 7 and beyond together).
+    const int nb = std::min(nprobe, 8);
     // Candidate pool of the tensor-core route: as the flat search's bf16 pool (3k, at least
     // k + max(k/4, 22)); up to 128 it fits one list per (query, probe). Larger k: the exact scan.
     const int pool = std::max(3 * k, k + std::max(k / 4, 22));
@@ -656,7 +663,7 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     // Scratch: probes + their distances, then the route's arrays (sized after the plan).
     const size_t pb = round_up(m * 4, 256);
     void* ws;
-    const size_t head = 2 * pb + round_up((int64_t)nlist * nprobe * 4, 256);
+    const size_t head = 2 * pb + round_up((int64_t)nlist * nb * 4, 256);
     VA_TRY(scratch(ctx, ivf, head, 0, &ws));
     uint32_t* probes = (uint32_t*)ws;
     float* pv = (float*)((uint8_t*)ws + pb);
@@ -685,15 +692,15 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
         VA_TRY(va_check_launch("k_ivf_scan"));
         return va_merge_lists_internal(ctx, cv, ci, nprobe, nq * k, k, nq, k, VA_SELECT_MIN, out_vals, out_ids);
     }
-    // Pairs per (list, probe rank), read back: the query tiles are laid out on the host.
-    const int64_t nls = (int64_t)nlist * nprobe;
+    // Pairs per (list, rank bucket), read back: the query tiles are laid out on the host.
+    const int64_t nls = (int64_t)nlist * nb;
     VA_CUDA_TRY(cudaMemsetAsync(cnt, 0, (size_t)nls * 4, ctx->stream));
-    k_probe_hist<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, cnt);
+    k_probe_hist<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, nb, cnt);
     VA_TRY(va_check_launch("k_probe_hist"));
     std::vector<int> h_cnt((size_t)nls);
     VA_CUDA_TRY(cudaMemcpyAsync(h_cnt.data(), cnt, (size_t)nls * 4, cudaMemcpyDeviceToHost, ctx->stream));
     VA_TRY(va_synchronize(ctx));
-    // A list's pairs in probe-rank order, cut into query tiles of 128. Tiles run by the rank of
+    // A list's pairs in rank-bucket order, cut into query tiles of 128. Tiles run by the bucket of
     // their first pair, then longest list first: the first rounds of the persistent grid scan
     // the queries' nearest lists, whose candidates set the per-query bounds that prune the
     // farther lists' tiles. (Rank-0 pairs in tiles of their own, run in a first launch so that
@@ -707,15 +714,15 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     std::vector<TileKey> keys;
     for (int L = 0; L < nlist; ++L) {
         int acc = 0;
-        for (int r = 0; r < nprobe; ++r) {
-            base[(size_t)L * nprobe + r] = acc;
-            acc += h_cnt[(size_t)L * nprobe + r];
+        for (int r = 0; r < nb; ++r) {
+            base[(size_t)L * nb + r] = acc;
+            acc += h_cnt[(size_t)L * nb + r];
         }
         lt0[(size_t)L] = (int)keys.size();
         const int64_t rows = ivf->h_offsets[(size_t)L + 1] - ivf->h_offsets[(size_t)L];
         int r = 0;
         for (int j = 0; j * 128 < acc; ++j) {
-            while (r + 1 < nprobe && base[(size_t)L * nprobe + r + 1] <= j * 128) ++r;
+            while (r + 1 < nb && base[(size_t)L * nb + r + 1] <= j * 128) ++r;
             keys.push_back({r, rows, L, j});
         }
     }
@@ -767,8 +774,8 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_CUDA_TRY(cudaMemcpyAsync(d_tiles, tile_list.data(), (size_t)n_qtiles * 4, cudaMemcpyHostToDevice, ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(cursor, 0, (size_t)nls * 4, ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(gmap, 0xFF, (size_t)G * 4, ctx->stream));
-    k_probe_scatter<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, d_base, cursor, d_lt0, d_tof, gmap,
-                                                          ginv);
+    k_probe_scatter<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, nb, d_base, cursor, d_lt0, d_tof,
+                                                          gmap, ginv);
     VA_TRY(va_check_launch("k_probe_scatter"));
     k_rows_bf16<<<grid_for(G * ivf->dpad), 256, 0, ctx->stream>>>(queries, G, ivf->dim, ivf->dpad, gmap, nprobe, qop);
     VA_TRY(va_check_launch("k_rows_bf16"));
