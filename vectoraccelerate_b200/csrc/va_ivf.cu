@@ -20,6 +20,8 @@
 
 #include <cuda_bf16.h>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include "va_internal.cuh"
 #include "va_tc.cuh"
 
@@ -112,53 +114,21 @@ __global__ void k_histogram(const uint32_t* __restrict__ assign, int64_t n, unsi
         atomicAdd(counts + assign[i], 1ull);
 }
 
-// Stable positions in list order: one block per list walks the assignments in row order, so the
-// rows of a list keep their relative order (ties in the scan then resolve by the original id as
-// in a flat search). pos[r] = the row's index in list order; ids_out[pos] = r + id_base.
-__global__ void k_list_positions(int64_t n, const uint32_t* __restrict__ assign, const int64_t* __restrict__ offsets,
-                                 int64_t* __restrict__ pos, uint32_t* __restrict__ ids_out, uint32_t id_base) {
-    const uint32_t c = blockIdx.x;
-    __shared__ int64_t s_pos;
-    __shared__ int s_warp[32];
-    __shared__ int s_cnt;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) s_pos = offsets[c];
-    __syncthreads();
-    for (int64_t base = 0; base < n; base += blockDim.x) {
-        const int64_t r = base + threadIdx.x;
-        const bool mine = r < n && assign[r] == c;
-        const unsigned bal = __ballot_sync(0xFFFFFFFFu, mine);
-        if (lane == 0) s_warp[warp] = __popc(bal);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int acc = 0;
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-                const int t = s_warp[w];
-                s_warp[w] = acc;
-                acc += t;
-            }
-            s_cnt = acc;
-        }
-        __syncthreads();
-        if (mine) {
-            const int64_t at = s_pos + s_warp[warp] + __popc(bal & ((1u << lane) - 1u));
-            pos[r] = at;
-            ids_out[at] = (uint32_t)r + id_base;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) s_pos += s_cnt;
-        __syncthreads();
-    }
+__global__ void k_iota(uint32_t* __restrict__ v, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        v[i] = (uint32_t)i;
 }
 
-// rows_out[pos[r]] = x[r], one warp per row.
-__global__ void k_place_rows(const float* __restrict__ x, int64_t n, int dim, const int64_t* __restrict__ pos,
-                             float* __restrict__ rows_out) {
-    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// Position p of the list-ordered copy takes row src[p] (rows sorted stably by list): a warp per
+// position copies the row; ids_out[p] = src[p] + id_base.
+__global__ void k_place_sorted(const float* __restrict__ x, const uint32_t* __restrict__ src, int64_t n, int dim,
+                               uint32_t id_base, float* __restrict__ rows_out, uint32_t* __restrict__ ids_out) {
+    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (r >= n) return;
-    const int64_t o = pos[r];
-    for (int j = lane; j < dim; j += 32) rows_out[o * dim + j] = x[r * dim + j];
+    if (p >= n) return;
+    const int64_t r = src[p];
+    for (int j = lane; j < dim; j += 32) rows_out[p * dim + j] = x[r * dim + j];
+    if (lane == 0) ids_out[p] = (uint32_t)r + id_base;
 }
 
 // out[r] = bf16 of src row map(r) zero padded to dpad (a zero row when map(r) < 0). map = null:
@@ -504,6 +474,7 @@ int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const 
     VA_REQUIRE(n > 0 && dim > 0 && dim <= VA_MAX_DIM && nlist > 0, "n, dim (<= %d) and nlist must be positive",
                VA_MAX_DIM);
     VA_REQUIRE((uint64_t)n + id_base <= 0xFFFFFFFFull, "numVectors + id_base exceeds the uint32 id range");
+    VA_REQUIRE(n < ((int64_t)1 << 31), "numVectors must stay below 2^31 per IVF index, got %lld", (long long)n);
     *out = nullptr;
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     va_ivf* ivf = new va_ivf();
@@ -528,17 +499,32 @@ int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const 
         return fail(va_set_error(VA_ERR_CUDA, "centroid copy failed"));
     int st = va_db_create(ctx, ivf->centroids, 1, nlist, dim, VA_DTYPE_F32, 0, &ivf->cdb);
     if (st != VA_OK) return fail(st);
-    // Assign every row, count the lists, prefix-sum the offsets on the host, scatter in order.
+    // Assign every row, count the lists (offsets by a prefix sum on the host), sort the row
+    // numbers by list with a stable radix sort (rows keep their order within a list), gather.
+    int end_bit = 1;
+    while (end_bit < 32 && ((uint64_t)1 << end_bit) < (uint64_t)nlist) ++end_bit;
+    size_t temp_bytes = 0;
+    if (cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                        (const uint32_t*)nullptr, (uint32_t*)nullptr, (int)n, 0, end_bit,
+                                        ctx->stream) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(va_set_error(VA_ERR_CUDA, "radix sort sizing failed"));
+    }
     void* ws = nullptr;
-    const size_t bytes = round_up(n * 4, 256) * 2 + round_up(n * 8, 256) + (size_t)nlist * 8 + 256;
+    const size_t nb4 = round_up(n * 4, 256);
+    const size_t bytes = nb4 * 5 + round_up((int64_t)nlist * 8, 256) + temp_bytes + 256;
     if (cudaMalloc(&ws, bytes) != cudaSuccess) {
         cudaGetLastError();
         return fail(va_set_error(VA_ERR_OOM, "IVF build scratch failed"));
     }
-    uint32_t* assign = (uint32_t*)ws;
-    float* vals = (float*)((uint8_t*)ws + round_up(n * 4, 256));
-    int64_t* pos = (int64_t*)((uint8_t*)vals + round_up(n * 4, 256));
-    unsigned long long* counts = (unsigned long long*)((uint8_t*)pos + round_up(n * 8, 256));
+    uint8_t* w8 = (uint8_t*)ws;
+    uint32_t* assign = (uint32_t*)w8;
+    float* vals = (float*)(w8 + nb4);
+    uint32_t* keys_out = (uint32_t*)(w8 + 2 * nb4);
+    uint32_t* src_in = (uint32_t*)(w8 + 3 * nb4);
+    uint32_t* src_out = (uint32_t*)(w8 + 4 * nb4);
+    unsigned long long* counts = (unsigned long long*)(w8 + 5 * nb4);
+    void* temp = w8 + 5 * nb4 + round_up((int64_t)nlist * 8, 256);
     st = assign_rows(ctx, ivf->cdb, rows, n, assign, vals);
     if (st == VA_OK) {
         cudaMemsetAsync(counts, 0, (size_t)nlist * 8, ctx->stream);
@@ -551,9 +537,16 @@ int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const 
             for (int c = 0; c < nlist; ++c) ivf->h_offsets[(size_t)c + 1] = ivf->h_offsets[(size_t)c] + (int64_t)h[(size_t)c];
             cudaMemcpyAsync(ivf->offsets, ivf->h_offsets.data(), (size_t)(nlist + 1) * 8, cudaMemcpyHostToDevice,
                             ctx->stream);
-            k_list_positions<<<nlist, 1024, 0, ctx->stream>>>(n, assign, ivf->offsets, pos, ivf->ids, id_base);
-            k_place_rows<<<(unsigned)((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(rows, n, dim, pos, ivf->rows);
-            st = va_check_launch("k_place_rows");
+            k_iota<<<grid_for(n), 256, 0, ctx->stream>>>(src_in, n);
+            if (cub::DeviceRadixSort::SortPairs(temp, temp_bytes, assign, keys_out, src_in, src_out, (int)n, 0, end_bit,
+                                                ctx->stream) != cudaSuccess) {
+                cudaGetLastError();
+                st = va_set_error(VA_ERR_CUDA, "radix sort of the list assignment failed");
+            } else {
+                k_place_sorted<<<(unsigned)((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(rows, src_out, n, dim,
+                                                                                         id_base, ivf->rows, ivf->ids);
+                st = va_check_launch("k_place_sorted");
+            }
         }
     }
     if (st == VA_OK) st = va_synchronize(ctx);
