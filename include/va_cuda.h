@@ -336,11 +336,12 @@ int va_ivf_list_sizes(const va_ivf* ivf, int64_t* sizes);
 /* Approximate k-NN (IVFSearchPipeline.search, :197-570): each query's nprobe nearest centroids
  * (ties by list id), then the k best rows of those lists by exact squared L2 and (distance, id),
  * sorted best-first; missing results are (+inf, 0xFFFFFFFF). queries [nq x dim], outputs
- * [nq x k], all device; k <= 128. For k <= 42 the lists are scanned on the tensor cores (the
- * queries of each list gathered into tiles of 128, bf16 keys, a per-query bound shared by its
- * probes) and a pool of max(3k, k + 22) candidates is reranked exactly; the tile layout is read
- * back (the call waits for the coarse step). Larger k: an exact fp64 scan, nq <= 65535. The
- * index keeps one search scratch: one search at a time per index. */
+ * [nq x k], all device; k <= 128. For k <= 103 the lists are scanned on the tensor cores (the
+ * queries of each list gathered into tiles of 128, a per-query bound shared by its probes) and a
+ * candidate pool is reranked exactly: bf16 keys and max(3k, k + 22) candidates up to k = 42, tf32
+ * keys and k + max(k/4, 22) candidates beyond; the tile layout is read back (the call waits for
+ * the coarse step). Larger k: an exact fp64 scan, nq <= 65535. The index keeps one search
+ * scratch: one search at a time per index. */
 int va_ivf_search(va_context* ctx, const va_ivf* ivf, const float* queries, int64_t nq, int k, int nprobe,
                   float* out_vals, uint32_t* out_ids);
 /* Same with HOST query and result buffers (copies in, searches, copies out, waits). The whole

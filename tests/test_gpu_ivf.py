@@ -18,11 +18,13 @@ def _true_vals(q, x_by_id, ids):
     return out
 
 
-# k <= 42 takes the tensor-core list scan (bf16 filter + exact rerank), larger k the exact fp64
-# scan; both must give the oracle's answer.
+# k <= 42 takes the tensor-core list scan with bf16 keys, 43 <= k <= 103 with tf32 keys (both an
+# exact rerank of a candidate pool), larger k the exact fp64 scan; all must give the oracle's
+# answer.
 @pytest.mark.parametrize("dim,nlist,nprobe,k", [(64, 32, 1, 10), (64, 32, 4, 10), (96, 16, 16, 100),
                                                 (128, 64, 8, 128), (7, 10, 3, 5), (64, 32, 8, 42),
-                                                (48, 20, 5, 43), (200, 40, 40, 1)])
+                                                (48, 20, 5, 43), (200, 40, 40, 1), (100, 24, 6, 103),
+                                                (64, 32, 8, 104), (128, 32, 4, 60)])
 def test_ivf_search_parity(ctx, oracle, dim, nlist, nprobe, k):
     import vectoraccelerate_b200 as va
     from oracle import ivf as O

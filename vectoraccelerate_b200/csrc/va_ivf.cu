@@ -44,6 +44,8 @@ struct va_ivf {
     // biases |x|^2 for n + 512 rows (+inf past n: a list's last tile may reach 255 rows beyond it).
     int dpad = 0;
     uint16_t* op = nullptr;
+    float* op32 = nullptr;        // fp32 operand [n x dpad] for the tf32 route: the rows when dim = dpad
+    bool op32_owned = false;
     float* bias = nullptr;
     // Search scratch, grown on demand (one search at a time per index).
     void* scratch = nullptr;
@@ -131,10 +133,15 @@ __global__ void k_place_sorted(const float* __restrict__ x, const uint32_t* __re
     if (lane == 0) ids_out[p] = (uint32_t)r + id_base;
 }
 
-// out[r] = bf16 of src row map(r) zero padded to dpad (a zero row when map(r) < 0). map = null:
-// row r; else row map[r] / map_div (gathered (query, probe) pairs -> their query).
-__global__ void k_rows_bf16(const float* __restrict__ src, int64_t n_out, int dim, int dpad,
-                            const int* __restrict__ map, int map_div, uint16_t* __restrict__ out) {
+__device__ __forceinline__ void store_op(uint16_t* p, float v) { *p = __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ void store_op(float* p, float v) { *p = v; }
+
+// out[r] = src row map(r) zero padded to dpad, as bf16 (T = uint16_t) or fp32 (a zero row when
+// map(r) < 0). map = null: row r; else row map[r] / map_div (gathered (query, probe) pairs -> their
+// query).
+template <class T>
+__global__ void k_rows_op(const float* __restrict__ src, int64_t n_out, int dim, int dpad,
+                          const int* __restrict__ map, int map_div, T* __restrict__ out) {
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_out * dpad;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = e / dpad;
@@ -142,7 +149,7 @@ __global__ void k_rows_bf16(const float* __restrict__ src, int64_t n_out, int di
         int64_t sr = r;
         if (map) sr = map[r] >= 0 ? map[r] / map_div : -1;
         const float v = (sr >= 0 && j < dim) ? src[sr * dim + j] : 0.f;
-        out[e] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+        store_op(out + e, v);
     }
 }
 
@@ -330,9 +337,9 @@ int prepare_operand(va_context* ctx, va_ivf* ivf) {
         return va_set_error(VA_ERR_OOM, "IVF operand allocation failed: %s", cudaGetErrorString(e));
     }
     if (n) {
-        k_rows_bf16<<<grid_for(n * ivf->dpad), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, ivf->dpad, nullptr, 1,
-                                                                       ivf->op);
-        VA_TRY(va_check_launch("k_rows_bf16"));
+        k_rows_op<uint16_t><<<grid_for(n * ivf->dpad), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, ivf->dpad,
+                                                                               nullptr, 1, ivf->op);
+        VA_TRY(va_check_launch("k_rows_op"));
     }
     k_row_norms<<<(unsigned)(((n + 512) * 32 + 255) / 256), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, n + 512,
                                                                                   ivf->bias);
@@ -622,6 +629,7 @@ int va_ivf_destroy(va_ivf* ivf) {
     if (ivf->ids) cudaFree(ivf->ids);
     if (ivf->offsets) cudaFree(ivf->offsets);
     if (ivf->op) cudaFree(ivf->op);
+    if (ivf->op32 && ivf->op32_owned) cudaFree(ivf->op32);
     if (ivf->bias) cudaFree(ivf->bias);
     if (ivf->scratch) cudaFree(ivf->scratch);
     delete ivf;
@@ -647,9 +655,12 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
                (long long)m);
     // Pairs are ordered by probe rank in up to 8 buckets (ranks 7 and beyond together).
     const int nb = std::min(nprobe, 8);
-    // Candidate pool of the tensor-core route: as the flat search's bf16 pool (3k, at least
-    // k + max(k/4, 22)); up to 128 it fits one list per (query, probe). Larger k: the exact scan.
-    const int pool = std::max(3 * k, k + std::max(k / 4, 22));
+    // Candidate pool of the tensor-core route, as the flat search's: bf16 keys with 3k (at least
+    // k + max(k/4, 22)) while that fits one list of 128 per (query, probe) (k <= 42), then tf32
+    // keys (4x smaller error) with k + max(k/4, 22) (k <= 103). Larger k: the exact scan.
+    const int pool_bf = std::max(3 * k, k + std::max(k / 4, 22)), pool_tf = k + std::max(k / 4, 22);
+    const int elem = pool_bf <= 128 ? 2 : 4;
+    const int pool = elem == 2 ? pool_bf : pool_tf;
     const bool tc = pool <= 128 && ivf->n > 0;
     const int kp = pool <= 32 ? 32 : pool <= 64 ? 64 : 128;
     const int nlist = ivf->nlist;
@@ -742,7 +753,8 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     };
     const size_t o_base = take((size_t)nls * 4), o_cur = take((size_t)nls * 4), o_lt0 = take((size_t)nlist * 4),
                  o_tof = take((size_t)n_qtiles * 4), o_tiles = take((size_t)n_qtiles * 4),
-                 o_gmap = take((size_t)G * 4), o_ginv = take((size_t)m * 8), o_qop = take((size_t)G * ivf->dpad * 2),
+                 o_gmap = take((size_t)G * 4), o_ginv = take((size_t)m * 8),
+                 o_qop = take((size_t)G * ivf->dpad * elem),
                  o_pk = take((size_t)G * kp * 4), o_pi = take((size_t)G * kp * 4);
     // (Bound levels fed by the probes, a probe's rank picking its slot, measured 4% slower: the
     // nearest list's kp-th key already prunes most of the farther lists.)
@@ -757,7 +769,7 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     int* d_tiles = (int*)(sb + o_tiles);
     int* gmap = (int*)(sb + o_gmap);
     int64_t* ginv = (int64_t*)(sb + o_ginv);
-    uint16_t* qop = (uint16_t*)(sb + o_qop);
+    void* qop = sb + o_qop;
     float* pk = (float*)(sb + o_pk);
     uint32_t* pi = (uint32_t*)(sb + o_pi);
     uint32_t* gthr = (uint32_t*)(sb + o_thr);
@@ -770,12 +782,33 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     k_probe_scatter<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, nb, d_base, cursor, d_lt0, d_tof,
                                                           gmap, ginv);
     VA_TRY(va_check_launch("k_probe_scatter"));
-    k_rows_bf16<<<grid_for(G * ivf->dpad), 256, 0, ctx->stream>>>(queries, G, ivf->dim, ivf->dpad, gmap, nprobe, qop);
-    VA_TRY(va_check_launch("k_rows_bf16"));
+    if (elem == 2)
+        k_rows_op<uint16_t><<<grid_for(G * ivf->dpad), 256, 0, ctx->stream>>>(queries, G, ivf->dim, ivf->dpad, gmap,
+                                                                               nprobe, (uint16_t*)qop);
+    else
+        k_rows_op<float><<<grid_for(G * ivf->dpad), 256, 0, ctx->stream>>>(queries, G, ivf->dim, ivf->dpad, gmap,
+                                                                            nprobe, (float*)qop);
+    VA_TRY(va_check_launch("k_rows_op"));
+    if (elem == 4 && !ivf->op32) {
+        // The fp32 operand, on first use: the rows themselves when they need no padding.
+        if (ivf->dim == ivf->dpad) {
+            ivf->op32 = ivf->rows;
+        } else {
+            if (cudaMalloc((void**)&ivf->op32, (size_t)ivf->n * ivf->dpad * 4) != cudaSuccess) {
+                cudaGetLastError();
+                ivf->op32 = nullptr;
+                return va_set_error(VA_ERR_OOM, "IVF fp32 operand allocation failed");
+            }
+            ivf->op32_owned = true;
+            k_rows_op<float><<<grid_for(ivf->n * ivf->dpad), 256, 0, ctx->stream>>>(ivf->rows, ivf->n, ivf->dim,
+                                                                                     ivf->dpad, nullptr, 1, ivf->op32);
+            VA_TRY(va_check_launch("k_rows_op"));
+        }
+    }
     TcFilterArgs a = {};
     a.q_op = qop;
-    a.x_op = ivf->op;
-    a.elem_bytes = 2;
+    a.x_op = elem == 2 ? (const void*)ivf->op : (const void*)ivf->op32;
+    a.elem_bytes = elem;
     a.dpad = ivf->dpad;
     a.n_rows = ivf->n;
     a.row_bias = ivf->bias;

@@ -1290,18 +1290,19 @@ int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, int
                        bool reset_bounds) {
     if (tiles <= 0) return VA_OK;
     VA_REQUIRE(kp == 32 || kp == 64 || kp == 128, "list length %d not supported", kp);
-    VA_REQUIRE(a.elem_bytes == 2, "list mode takes bf16 operands");
+    VA_REQUIRE(a.elem_bytes == 2 || a.elem_bytes == 4, "list mode takes bf16 or fp32 (tf32) operands");
+    const int elem = a.elem_bytes;
     VA_REQUIRE(tile0 >= 0 && tile0 + tiles <= n_qtiles, "tile range [%d, %d) outside %d tiles", tile0, tile0 + tiles,
                n_qtiles);
     CUtensorMap mq, mx;
     const int64_t nq_pad = (int64_t)n_qtiles * BM;
-    VA_TRY(make_tmap(&mq, a.q_op, nq_pad, a.dpad, 2, BM));
-    VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, 2, BN));
+    VA_TRY(make_tmap(&mq, a.q_op, nq_pad, a.dpad, elem, BM));
+    VA_TRY(make_tmap(&mx, a.x_op, a.n_rows, a.dpad, elem, BN));
     Work w = {};
     w.n_qtiles = tiles;
     w.splits = 1;
     w.n_tiles = 0;
-    w.k_blocks = (int)((a.dpad * 2 + BKB - 1) / BKB);
+    w.k_blocks = (int)((a.dpad * elem + BKB - 1) / BKB);
     w.n_rows = a.n_rows;
     w.nq_pad = nq_pad;
     w.chunk_tiles = 1;
@@ -1318,6 +1319,11 @@ int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, int
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "list length %d too large for shared memory", kp);
     const size_t smem = smem_bytes(kp, stages, false);
     const int grid = std::min(tiles, ctx->sm_count);
+    if (elem == 4) {
+        if (kp == 32) return launch_filter<4, 32>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
+        if (kp == 64) return launch_filter<4, 64>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
+        return launch_filter<4, 128>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
+    }
     if (kp == 32) return launch_filter<2, 32>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
     if (kp == 64) return launch_filter<2, 64>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
     return launch_filter<2, 128>(ctx, a, stages, smem, mq, mx, w, grid, false, reset_bounds);
