@@ -47,9 +47,12 @@ struct va_ivf {
     float* op32 = nullptr;        // fp32 operand [n x dpad] for the tf32 route: the rows when dim = dpad
     bool op32_owned = false;
     float* bias = nullptr;
-    // Search scratch, grown on demand (one search at a time per index).
+    // Search scratch, grown on demand (one search at a time per index), and pinned host memory
+    // for the tile plan (the count read-back and one upload).
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    int* h_plan = nullptr;
+    size_t h_plan_ints = 0;
 };
 
 namespace {
@@ -632,6 +635,7 @@ int va_ivf_destroy(va_ivf* ivf) {
     if (ivf->op32 && ivf->op32_owned) cudaFree(ivf->op32);
     if (ivf->bias) cudaFree(ivf->bias);
     if (ivf->scratch) cudaFree(ivf->scratch);
+    if (ivf->h_plan) cudaFreeHost(ivf->h_plan);
     delete ivf;
     return VA_OK;
 }
@@ -681,7 +685,7 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
                                                                                      : VA_PREC_AUTO;
     VA_TRY(va_knn_search(ctx, ivf->cdb, queries, nq, nprobe, VA_METRIC_L2SQ, cprec, 0, pv, probes));
     if (!tc) {
-        VA_REQUIRE(nq <= 65535, "numQueries %lld exceeds 65535 per IVF call for k > 42", (long long)nq);
+        VA_REQUIRE(nq <= 65535, "numQueries %lld exceeds 65535 per IVF call for k > 103", (long long)nq);
         const size_t lb = (size_t)m * k;
         VA_TRY(scratch(ctx, ivf, pb + lb * 8 + 256, pb, &ws));  // the probes move along
         probes = (uint32_t*)ws;
@@ -701,28 +705,46 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_CUDA_TRY(cudaMemsetAsync(cnt, 0, (size_t)nls * 4, ctx->stream));
     k_probe_hist<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, nb, cnt);
     VA_TRY(va_check_launch("k_probe_hist"));
-    std::vector<int> h_cnt((size_t)nls);
-    VA_CUDA_TRY(cudaMemcpyAsync(h_cnt.data(), cnt, (size_t)nls * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    // Pinned plan buffer: [counts | base | lt0 | tile_of | tile_list], tiles at most m/128 + nlist.
+    const int64_t nt_max = m / 128 + nlist + 1;
+    const size_t plan_ints = (size_t)(2 * nls + nlist + 2 * nt_max);
+    if (plan_ints > ivf->h_plan_ints) {
+        if (ivf->h_plan) cudaFreeHost(ivf->h_plan);
+        ivf->h_plan = nullptr;
+        ivf->h_plan_ints = 0;
+        if (cudaHostAlloc((void**)&ivf->h_plan, plan_ints * 4, cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            ivf->h_plan = nullptr;
+            return va_set_error(VA_ERR_OOM, "pinned IVF plan buffer of %zu bytes failed", plan_ints * 4);
+        }
+        ivf->h_plan_ints = plan_ints;
+    }
+    int* h_cnt = ivf->h_plan;
+    int* base = h_cnt + nls;
+    int* lt0 = base + nls;
+    int* tile_of = lt0 + nlist;
+    int* tile_list = tile_of + nt_max;
+    VA_CUDA_TRY(cudaMemcpyAsync(h_cnt, cnt, (size_t)nls * 4, cudaMemcpyDeviceToHost, ctx->stream));
     VA_TRY(va_synchronize(ctx));
     // A list's pairs in rank-bucket order, cut into query tiles of 128. Tiles run by the bucket of
     // their first pair, then longest list first: the first rounds of the persistent grid scan
     // the queries' nearest lists, whose candidates set the per-query bounds that prune the
     // farther lists' tiles. (Rank-0 pairs in tiles of their own, run in a first launch so that
     // every bound is set before the rest, measured slower: 30% more tiles, mostly padding.)
-    std::vector<int> base((size_t)nls), lt0((size_t)nlist, 0);
     struct TileKey {
         int rank;
         int64_t rows;
         int list, j;
     };
     std::vector<TileKey> keys;
+    keys.reserve((size_t)nt_max);
     for (int L = 0; L < nlist; ++L) {
         int acc = 0;
         for (int r = 0; r < nb; ++r) {
             base[(size_t)L * nb + r] = acc;
             acc += h_cnt[(size_t)L * nb + r];
         }
-        lt0[(size_t)L] = (int)keys.size();
+        lt0[L] = (int)keys.size();
         const int64_t rows = ivf->h_offsets[(size_t)L + 1] - ivf->h_offsets[(size_t)L];
         int r = 0;
         for (int j = 0; j * 128 < acc; ++j) {
@@ -737,24 +759,22 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
         const TileKey &a = keys[(size_t)x], &b = keys[(size_t)y];
         return a.rank != b.rank ? a.rank < b.rank : a.rows > b.rows;
     });
-    std::vector<int> tile_list((size_t)n_qtiles), tile_of((size_t)n_qtiles);
     for (int t = 0; t < n_qtiles; ++t) {
         const TileKey& kt = keys[(size_t)ord[(size_t)t]];
-        tile_list[(size_t)t] = kt.list;
-        tile_of[(size_t)(lt0[(size_t)kt.list] + kt.j)] = t;
+        tile_list[t] = kt.list;
+        tile_of[lt0[kt.list] + kt.j] = t;
     }
     const int64_t G = (int64_t)n_qtiles * 128;
-    // Scratch layout after the probes and counts.
+    // Scratch layout after the probes and counts; the plan keeps the pinned buffer's layout.
     size_t off = head;
     auto take = [&](size_t bytes) {
         const size_t o = off;
         off += round_up((int64_t)bytes, 256);
         return o;
     };
-    const size_t o_base = take((size_t)nls * 4), o_cur = take((size_t)nls * 4), o_lt0 = take((size_t)nlist * 4),
-                 o_tof = take((size_t)n_qtiles * 4), o_tiles = take((size_t)n_qtiles * 4),
-                 o_gmap = take((size_t)G * 4), o_ginv = take((size_t)m * 8),
-                 o_qop = take((size_t)G * ivf->dpad * elem),
+    const size_t plan_up = (size_t)(nls + nlist + 2 * nt_max) * 4;
+    const size_t o_plan = take(plan_up), o_cur = take((size_t)nls * 4), o_gmap = take((size_t)G * 4),
+                 o_ginv = take((size_t)m * 8), o_qop = take((size_t)G * ivf->dpad * elem),
                  o_pk = take((size_t)G * kp * 4), o_pi = take((size_t)G * kp * 4);
     // (Bound levels fed by the probes, a probe's rank picking its slot, measured 4% slower: the
     // nearest list's kp-th key already prunes most of the farther lists.)
@@ -762,21 +782,18 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_TRY(scratch(ctx, ivf, off, pb, &ws));  // the probes move along
     uint8_t* sb = (uint8_t*)ws;
     probes = (uint32_t*)sb;
-    int* d_base = (int*)(sb + o_base);
+    int* d_base = (int*)(sb + o_plan);
+    int* d_lt0 = d_base + nls;
+    int* d_tof = d_lt0 + nlist;
+    int* d_tiles = d_tof + nt_max;
     int* cursor = (int*)(sb + o_cur);
-    int* d_lt0 = (int*)(sb + o_lt0);
-    int* d_tof = (int*)(sb + o_tof);
-    int* d_tiles = (int*)(sb + o_tiles);
     int* gmap = (int*)(sb + o_gmap);
     int64_t* ginv = (int64_t*)(sb + o_ginv);
     void* qop = sb + o_qop;
     float* pk = (float*)(sb + o_pk);
     uint32_t* pi = (uint32_t*)(sb + o_pi);
     uint32_t* gthr = (uint32_t*)(sb + o_thr);
-    VA_CUDA_TRY(cudaMemcpyAsync(d_base, base.data(), (size_t)nls * 4, cudaMemcpyHostToDevice, ctx->stream));
-    VA_CUDA_TRY(cudaMemcpyAsync(d_lt0, lt0.data(), (size_t)nlist * 4, cudaMemcpyHostToDevice, ctx->stream));
-    VA_CUDA_TRY(cudaMemcpyAsync(d_tof, tile_of.data(), (size_t)n_qtiles * 4, cudaMemcpyHostToDevice, ctx->stream));
-    VA_CUDA_TRY(cudaMemcpyAsync(d_tiles, tile_list.data(), (size_t)n_qtiles * 4, cudaMemcpyHostToDevice, ctx->stream));
+    VA_CUDA_TRY(cudaMemcpyAsync(d_base, base, plan_up, cudaMemcpyHostToDevice, ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(cursor, 0, (size_t)nls * 4, ctx->stream));
     VA_CUDA_TRY(cudaMemsetAsync(gmap, 0xFF, (size_t)G * 4, ctx->stream));
     k_probe_scatter<<<grid_for(m), 256, 0, ctx->stream>>>(probes, m, nprobe, nb, d_base, cursor, d_lt0, d_tof,
