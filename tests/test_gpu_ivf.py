@@ -144,3 +144,22 @@ def test_kmeans_seeded_is_deterministic_and_converges(ctx, oracle):
         m = a.assignments == j
         if m.any():
             np.testing.assert_allclose(a.centroids[j], x[m].astype(np.float64).mean(axis=0), rtol=1e-4, atol=1e-5)
+
+
+def test_ivf_many_lists_coarse_tf32(ctx, oracle):
+    """More than 16,384 lists: the coarse quantizer takes the tensor-core (TF32) route. With the
+    rows themselves as centroids every list holds its own row, so probing the 8 nearest lists
+    returns the exact 8 nearest rows."""
+    import vectoraccelerate_b200 as va
+    x = oracle.gen_gaussian(20000, 32, 430)
+    q = oracle.gen_gaussian(12, 32, 431, row0=QROW)
+    pipe = va.IVFSearchPipeline(ctx, va.IVFSearchConfiguration(20000, 8, 32))
+    st = pipe.build(x, x)
+    try:
+        assert st.total_vectors == 20000 and int(st.list_sizes.max()) == 1
+        res = pipe.search(q, st, 8)
+        tids, tvals = oracle.knn(q, x, 8)
+        assert np.array_equal(res.indices, tids)
+        np.testing.assert_allclose(res.distances, tvals, rtol=1e-5, atol=1e-6)
+    finally:
+        st.close()

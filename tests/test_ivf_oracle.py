@@ -52,3 +52,22 @@ def test_probe_padding(oracle):
     for qi in range(3):
         n = int(np.sum(i[qi] != 0xFFFFFFFF))
         assert n <= 40 and np.all(np.isinf(v[qi, n:]))
+
+
+def test_ivf_configuration_validation():
+    """KMeansConfiguration / IVFSearchConfiguration reject what the reference rejects
+    (ClusteringKernels.swift:115-130, IVFKernels.swift:28-60); no GPU needed."""
+    import pytest
+
+    import vectoraccelerate_b200 as va
+    cfg = va.KMeansConfiguration(num_clusters=8, dimension=16)
+    assert cfg.max_iterations == 100 and cfg.convergence_threshold == 1e-4
+    for bad in (dict(num_clusters=0, dimension=16), dict(num_clusters=4, dimension=0),
+                dict(num_clusters=4, dimension=16, max_iterations=0),
+                dict(num_clusters=4, dimension=16, convergence_threshold=0.0)):
+        with pytest.raises(va.InvalidInput):
+            va.KMeansConfiguration(**bad)
+    assert va.IVFSearchConfiguration(16, 4, 32).nprobe == 4
+    for bad in ((0, 1, 8), (4, 0, 8), (4, 5, 8), (4, 2, 0)):
+        with pytest.raises(va.InvalidInput):
+            va.IVFSearchConfiguration(*bad)

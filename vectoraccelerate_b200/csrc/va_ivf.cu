@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(LS_THREADS) k_ivf_scan(const float* __restrict
             }
         }
         __syncthreads();
-        // Every thread reads the count before any warp of the next round adds to it.
+        // Every thread reads the count before any warp of the next pass over rows adds to it.
         const bool full = s_cnt > LS_BUF - nwarps;
         __syncthreads();
         if (full) compact();
