@@ -654,7 +654,7 @@ def run_ivf(a):
     iters = ctypes.c_int(0)
     t0 = time.perf_counter()
     _ffi.call("va_ivf_train", ctx.handle, x.data_ptr(), n, dim, nlist, a.kmeans_iters, ctypes.c_float(a.kmeans_tol),
-              42, 0, cent.data_ptr(), ctypes.byref(iters))
+              42, _ffi.IVF_INIT_KMEANSPP, cent.data_ptr(), ctypes.byref(iters))
     ctx.synchronize()
     t_train = time.perf_counter() - t0
     h = ctypes.c_void_p()
@@ -705,7 +705,7 @@ def run_ivf(a):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
         "dtype": "bf16 list scan + f64 exact rerank (fp32 coarse quantizer)",
         "data": "synthetic: mixture of 256 centroids sigma 0.5 (TestRNG restatement on the device)",
-        "config": {"workload": f"IVF k-NN: N={n:,} x d={dim} fp32, k-means {nlist} lists ({iters.value} iterations, "
+        "config": {"workload": f"IVF k-NN: N={n:,} x d={dim} fp32, k-means++ then Lloyd, {nlist} lists ({iters.value} iterations, "
                                f"{t_train:.2f} s), Q={nq:,}, k={k}, nprobe={nprobe}",
                    "config": "ivf", "N": n, "d": dim, "Q": nq, "k": k, "nlist": nlist, "nprobe": nprobe,
                    f"recall@{k}_vs_exact": recall,

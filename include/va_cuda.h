@@ -311,13 +311,16 @@ int va_hamming_knn_db(va_context* ctx, const va_database* db, const uint32_t* qu
 /* IVF index (IVFSearchPipeline, Index/Kernels/IVF/IVFSearchPipeline.swift:110-600; k-means      */
 /* training, Index/Kernels/Clustering/KMeansPipeline.swift:102-240). Squared L2, fp32 rows.     */
 /* ------------------------------------------------------------------------------------------ */
-/* k-means over x[n x dim] (device): initial centroids are nlist distinct rows drawn with `seed`
- * (or, with init_given != 0, the centroids out_centroids holds on entry), then Lloyd iterations
- * (exact assignment, mean update; an empty list keeps its centroid) until the largest centroid
- * movement is below tol or max_iters iterations ran. out_centroids [nlist x dim] (device);
- * out_iters (host, optional) = iterations run. */
+/* Initial centroids of va_ivf_train. */
+#define VA_IVF_INIT_KMEANSPP 0 /* k-means++ (KMeansPlusPlusKernel.swift:94-210), draws from `seed` */
+#define VA_IVF_INIT_GIVEN 1    /* the centroids out_centroids holds on entry */
+#define VA_IVF_INIT_RANDOM 2   /* nlist distinct rows drawn from `seed` */
+/* k-means over x[n x dim] (device): initial centroids per `init`, then Lloyd iterations (exact
+ * assignment, mean update; an empty list keeps its centroid) until the largest centroid movement
+ * is below tol or max_iters iterations ran. out_centroids [nlist x dim] (device); out_iters
+ * (host, optional) = iterations run. Deterministic for a given seed. */
 int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist, int max_iters, float tol,
-                 uint64_t seed, int init_given, float* out_centroids, int* out_iters);
+                 uint64_t seed, int init, float* out_centroids, int* out_iters);
 /* Build the inverted lists: every row of rows[n x dim] (device) goes to its nearest centroid
  * (ties to the lower list), rows are copied in list order (stable within a list), ids are
  * row + id_base (IVFSearchPipeline.prepareIndexStructure, :110-195). */

@@ -163,3 +163,32 @@ def test_ivf_many_lists_coarse_tf32(ctx, oracle):
         np.testing.assert_allclose(res.distances, tvals, rtol=1e-5, atol=1e-6)
     finally:
         st.close()
+
+
+def test_kmeanspp_seeds(ctx, oracle):
+    """k-means++ seeds (max_iters = 0): distinct rows of the data, the same for the same seed, and
+    on well-separated clusters one seed per cluster (D^2 sampling)."""
+    import ctypes
+
+    import vectoraccelerate_b200 as va
+    from vectoraccelerate_b200 import _ffi
+    rng = np.random.default_rng(5)
+    centers = rng.normal(size=(8, 16)).astype(np.float32) * 20
+    lab = np.repeat(np.arange(8), 500)
+    x = (centers[lab] + rng.normal(size=(4000, 16)).astype(np.float32) * 0.05).astype(np.float32)
+
+    def seeds(seed):
+        dx = ctx.get_buffer_for(x)
+        dc = ctx.get_buffer(8 * 16 * 4, np.float32, (8, 16))
+        it = ctypes.c_int(-1)
+        _ffi.call("va_ivf_train", ctx.handle, dx.ptr, 4000, 16, 8, 0, ctypes.c_float(1e-3), seed,
+                  _ffi.IVF_INIT_KMEANSPP, dc.ptr, ctypes.byref(it))
+        assert it.value == 0
+        return dc.download()
+
+    a, b, c = seeds(11), seeds(11), seeds(12)
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    rows = [int(np.where((x == s).all(axis=1))[0][0]) for s in a]   # every seed is a row
+    assert len(set(rows)) == 8 and sorted(set(lab[rows])) == list(range(8))
+    km = va.KMeansPipeline(ctx, va.KMeansConfiguration(num_clusters=8, dimension=16, max_iterations=20)).fit(x)
+    assert km.converged and len(set(km.assignments[lab == 0])) == 1

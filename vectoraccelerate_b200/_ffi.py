@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(_HERE, "libva_cuda.so")
 # Constants mirrored from va_cuda.h.
 VA_OK = 0
 METRIC_L2SQ, METRIC_COSINE, METRIC_IP = 0, 1, 2
+IVF_INIT_KMEANSPP, IVF_INIT_GIVEN, IVF_INIT_RANDOM = 0, 1, 2
 PREC_AUTO, PREC_FP32, PREC_TF32, PREC_BF16 = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16 = 0, 1
 SELECT_MIN, SELECT_MAX = 0, 1

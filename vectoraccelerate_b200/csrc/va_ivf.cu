@@ -8,14 +8,16 @@
 //     list), so each probed list is one contiguous range streamed once per (query, probe);
 //   * the coarse quantizer is the fused exact k-NN of the queries against the centroids
 //     (tensor-core filter + exact rerank), and k-means assignment is the same search with k = 1;
-//   * k-means starts from `nlist` distinct rows drawn with a seeded generator (the reference seeds
-//     with k-means++) and runs Lloyd iterations until the largest centroid movement is below
-//     `tol` (KMeansConvergenceKernel.swift:78-110), as the reference does.
+//   * k-means starts from k-means++ seeds, as the reference (KMeansPlusPlusKernel.swift), drawn
+//     with a seeded generator (or from given centroids, or distinct random rows), and runs Lloyd
+//     iterations until the largest centroid movement is below `tol`
+//     (KMeansConvergenceKernel.swift:78-110), as the reference does.
 // The list scan computes exact squared L2 (fp32 rows, fp64 accumulation) and keeps, per (query,
 // probe), the k best (distance, id) composites; the probes' lists are merged by (distance, id).
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <unordered_set>
 #include <vector>
 
 #include <cuda_bf16.h>
@@ -111,6 +113,68 @@ __global__ void k_max_movement(const float* __restrict__ a, const float* __restr
     }
     s = warp_sum_d(s);
     if (lane == 0) atomicMax(move_bits, __float_as_uint((float)s));
+}
+
+// k-means++ seeding (KMeansPlusPlusKernel.swift:94-210: first centroid uniform, then each next
+// one drawn with probability proportional to the squared distance to the nearest chosen one).
+// d2[r] = min(d2[r], |x_r - c|^2) for the newest centroid c (first: d2[r] = |x_r - c|^2), and
+// bsum[b] = the fp64 sum of d2 over block b's KPP_ROWS rows, in a fixed order (deterministic).
+constexpr int KPP_ROWS = 1024;
+__global__ void __launch_bounds__(256) k_kpp_update(const float* __restrict__ x, int64_t n, int dim,
+                                                    const float* __restrict__ c, int first, float* __restrict__ d2,
+                                                    double* __restrict__ bsum) {
+    __shared__ double s_w[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = (int64_t)blockIdx.x * KPP_ROWS;
+    double acc = 0;
+    for (int64_t r = r0 + warp; r < n && r < r0 + KPP_ROWS; r += 8) {
+        double s = 0;
+        for (int j = lane; j < dim; j += 32) {
+            const double t = (double)x[r * dim + j] - (double)c[j];
+            s += t * t;
+        }
+        s = warp_sum_d(s);
+        const float v = first ? (float)s : fminf(d2[r], (float)s);
+        if (lane == 0) {
+            d2[r] = v;
+            acc += (double)v;
+        }
+    }
+    if (lane == 0) s_w[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0;
+        for (int w = 0; w < 8; ++w) t += s_w[w];
+        bsum[blockIdx.x] = t;
+    }
+}
+
+// One warp: the first row r in [r0, r1) whose running fp64 sum of d2 from r0 reaches target
+// (the last row with d2 > 0 when rounding leaves the target just out of reach).
+__global__ void k_kpp_pick(const float* __restrict__ d2, int64_t r0, int64_t r1, double target,
+                           int64_t* __restrict__ out) {
+    const int lane = threadIdx.x;
+    double run = 0;
+    int64_t last_pos = -1;
+    for (int64_t b = r0; b < r1; b += 32) {
+        const int64_t r = b + lane;
+        const double v = r < r1 ? (double)d2[r] : 0.0;
+        double incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const unsigned hit = __ballot_sync(0xFFFFFFFFu, v > 0 && run + incl >= target);
+        const unsigned pos = __ballot_sync(0xFFFFFFFFu, v > 0);
+        if (pos) last_pos = b + 31 - __clz(pos);
+        if (hit) {
+            if (lane == 0) *out = b + __ffs(hit) - 1;
+            return;
+        }
+        run += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (lane == 0) *out = last_pos >= 0 ? last_pos : r0;
 }
 
 // ---------------------------------------------------------------------------------- lists
@@ -371,6 +435,70 @@ int scratch(va_context* ctx, va_ivf* ivf, size_t bytes, size_t keep, void** out)
     return VA_OK;
 }
 
+// Seeded generator of the initial centroids (64-bit LCG; uniform doubles from its top 53 bits).
+struct Lcg {
+    uint64_t s;
+    explicit Lcg(uint64_t seed) : s(seed * 6364136223846793005ull + 1442695040888963407ull) {}
+    uint64_t next() {
+        s = s * 6364136223846793005ull + 1442695040888963407ull;
+        return s;
+    }
+    double uniform() { return (double)(next() >> 11) * (1.0 / 9007199254740992.0); }
+};
+
+// k-means++ seeding into cent[nlist x dim]: per centroid one update of the squared distances
+// with a block-sum read back, the draw on the host (fp64 running sums over the blocks), and the
+// row picked inside the drawn block by one warp.
+int kmeanspp(va_context* ctx, const float* x, int64_t n, int dim, int nlist, Lcg& rng, float* cent) {
+    const int64_t nblocks = (n + KPP_ROWS - 1) / KPP_ROWS;
+    void* ws = nullptr;
+    const size_t bytes = round_up(n * 4, 256) + round_up(nblocks * 8, 256) + 256;
+    VA_CUDA_TRY(cudaMalloc(&ws, bytes));
+    float* d2 = (float*)ws;
+    double* bsum = (double*)((uint8_t*)ws + round_up(n * 4, 256));
+    int64_t* d_idx = (int64_t*)((uint8_t*)bsum + round_up(nblocks * 8, 256));
+    std::vector<double> h((size_t)nblocks);
+    int st = VA_OK;
+    int64_t idx = (int64_t)(rng.next() % (uint64_t)n);
+    for (int c = 0; c < nlist && st == VA_OK; ++c) {
+        if (c > 0) {
+            k_kpp_update<<<(unsigned)nblocks, 256, 0, ctx->stream>>>(x, n, dim, cent + (size_t)(c - 1) * dim, c == 1,
+                                                                     d2, bsum);
+            if ((st = va_check_launch("k_kpp_update")) != VA_OK) break;
+            if (cudaMemcpyAsync(h.data(), bsum, (size_t)nblocks * 8, cudaMemcpyDeviceToHost, ctx->stream) !=
+                cudaSuccess) {
+                st = va_set_error(VA_ERR_CUDA, "k-means++ read-back failed");
+                break;
+            }
+            if ((st = va_synchronize(ctx)) != VA_OK) break;
+            double total = 0;
+            for (double v : h) total += v;
+            if (!(total > 0)) {
+                idx = (int64_t)(rng.next() % (uint64_t)n);  // every row sits on a centroid
+            } else {
+                const double target = rng.uniform() * total;
+                double run = 0;
+                int64_t b = 0;
+                while (b + 1 < nblocks && run + h[(size_t)b] < target) run += h[(size_t)b++];
+                const int64_t r0 = b * KPP_ROWS, r1 = std::min<int64_t>(n, r0 + KPP_ROWS);
+                k_kpp_pick<<<1, 32, 0, ctx->stream>>>(d2, r0, r1, target - run, d_idx);
+                if ((st = va_check_launch("k_kpp_pick")) != VA_OK) break;
+                if (cudaMemcpyAsync(&idx, d_idx, 8, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess) {
+                    st = va_set_error(VA_ERR_CUDA, "k-means++ read-back failed");
+                    break;
+                }
+                if ((st = va_synchronize(ctx)) != VA_OK) break;
+            }
+        }
+        if (cudaMemcpyAsync(cent + (size_t)c * dim, x + idx * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice,
+                            ctx->stream) != cudaSuccess)
+            st = va_set_error(VA_ERR_CUDA, "k-means++ centroid copy failed");
+    }
+    if (st == VA_OK) st = va_synchronize(ctx);
+    cudaFree(ws);
+    return st;
+}
+
 // Assignment of every row to its nearest centroid (the fused search with k = 1).
 int assign_rows(va_context* ctx, va_database* cdb, const float* x, int64_t n, uint32_t* assign, float* scratch_v) {
     return va_knn_search(ctx, cdb, x, n, 1, VA_METRIC_L2SQ, VA_PREC_AUTO, 0, scratch_v, assign);
@@ -381,36 +509,35 @@ int assign_rows(va_context* ctx, va_database* cdb, const float* x, int64_t n, ui
 extern "C" {
 
 int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist, int max_iters, float tol,
-                 uint64_t seed, int init_given, float* out_centroids, int* out_iters) {
+                 uint64_t seed, int init, float* out_centroids, int* out_iters) {
     VA_REQUIRE(ctx && x && out_centroids, "ctx, x and out_centroids must not be NULL");
     VA_REQUIRE(dim > 0 && dim <= VA_MAX_DIM, "dimension must be in 1..%d, got %d", VA_MAX_DIM, dim);
     VA_REQUIRE(nlist > 0 && nlist <= n, "nlist must be in 1..numVectors (%lld), got %d", (long long)n, nlist);
     VA_REQUIRE(max_iters >= 0, "max_iters must be >= 0");
+    VA_REQUIRE(init == VA_IVF_INIT_KMEANSPP || init == VA_IVF_INIT_GIVEN || init == VA_IVF_INIT_RANDOM,
+               "init must be VA_IVF_INIT_KMEANSPP, _GIVEN or _RANDOM, got %d", init);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
-    // Initial centroids: nlist distinct rows, a seeded partial Fisher-Yates shuffle on the host.
-    std::vector<int64_t> pick((size_t)nlist);
-    {
-        uint64_t s = seed * 6364136223846793005ull + 1442695040888963407ull;
-        std::vector<int64_t> perm;
-        const bool dense = n <= (int64_t)nlist * 8;
-        if (dense) {
-            perm.resize((size_t)n);
+    Lcg rng(seed);
+    if (init == VA_IVF_INIT_KMEANSPP) VA_TRY(kmeanspp(ctx, x, n, dim, nlist, rng, out_centroids));
+    // Random initial centroids: nlist distinct rows (a partial Fisher-Yates shuffle when nlist is
+    // a large share of n, else rejection of repeats).
+    std::vector<int64_t> pick;
+    if (init == VA_IVF_INIT_RANDOM) {
+        pick.resize((size_t)nlist);
+        if (n <= (int64_t)nlist * 8) {
+            std::vector<int64_t> perm((size_t)n);
             for (int64_t i = 0; i < n; ++i) perm[(size_t)i] = i;
-        }
-        std::vector<int64_t> chosen;
-        for (int i = 0; i < nlist; ++i) {
-            s = s * 6364136223846793005ull + 1442695040888963407ull;
-            if (dense) {
-                const int64_t j = i + (int64_t)((s >> 17) % (uint64_t)(n - i));
+            for (int i = 0; i < nlist; ++i) {
+                const int64_t j = i + (int64_t)(rng.next() % (uint64_t)(n - i));
                 std::swap(perm[(size_t)i], perm[(size_t)j]);
                 pick[(size_t)i] = perm[(size_t)i];
-            } else {
+            }
+        } else {
+            std::unordered_set<int64_t> chosen;
+            for (int i = 0; i < nlist; ++i) {
                 int64_t r;
-                do {
-                    s = s * 6364136223846793005ull + 1442695040888963407ull;
-                    r = (int64_t)((s >> 17) % (uint64_t)n);
-                } while (std::find(chosen.begin(), chosen.end(), r) != chosen.end());
-                chosen.push_back(r);
+                do r = (int64_t)(rng.next() % (uint64_t)n);
+                while (!chosen.insert(r).second);
                 pick[(size_t)i] = r;
             }
         }
@@ -443,9 +570,10 @@ int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist,
         cudaFree(ws);
         return s;
     };
-    if (cudaMemcpyAsync(d_pick, pick.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
-        return fail(va_set_error(VA_ERR_CUDA, "upload failed"));
-    if (!init_given) {
+    if (init == VA_IVF_INIT_RANDOM) {
+        if (cudaMemcpyAsync(d_pick, pick.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, ctx->stream) !=
+            cudaSuccess)
+            return fail(va_set_error(VA_ERR_CUDA, "upload failed"));
         k_gather_rows_f32<<<grid_for((int64_t)cb), 256, 0, ctx->stream>>>(x, dim, d_pick, nlist, out_centroids);
         if ((st = va_check_launch("k_gather_rows_f32")) != VA_OK) return fail(st);
     }

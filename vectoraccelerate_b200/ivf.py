@@ -8,9 +8,10 @@ IVFKernels.swift:28-60). Squared L2 only, as the reference's IVF path. The compu
 assignment and the coarse quantizer run on the fused exact k-NN, the probed lists are scanned
 with exact squared L2, results are ordered by (distance, id).
 
-Differences from the reference, on purpose: k-means starts from ``num_clusters`` distinct rows
-drawn with a seeded generator instead of k-means++; ``IVFSearchPipeline.build`` forms the lists by
-nearest-centroid assignment on the device (the reference's callers form them on the host).
+Differences from the reference, on purpose: the k-means++ draws come from a seeded generator
+(deterministic; the reference uses the system generator), and ``init="random"`` offers distinct
+random rows instead; ``IVFSearchPipeline.build`` forms the lists by nearest-centroid assignment on
+the device (the reference's callers form them on the host).
 """
 
 from __future__ import annotations
@@ -43,8 +44,11 @@ class KMeansConfiguration:
     max_iterations: int = 100
     convergence_threshold: float = 1e-4
     seed: int = 42
+    init: str = "kmeans++"   # or "random" (distinct rows); given centroids go to fit()
 
     def __post_init__(self):
+        if self.init not in ("kmeans++", "random"):
+            raise InvalidInput(f"init must be 'kmeans++' or 'random', got {self.init!r}")
         if self.num_clusters < 1:
             raise InvalidInput(f"numClusters must be at least 1, got {self.num_clusters}")
         if self.dimension < 1:
@@ -81,15 +85,15 @@ class KMeansPipeline:
         dx = ctx.get_buffer_for(x)
         dc = ctx.get_buffer(4 * cfg.num_clusters * cfg.dimension, np.float32, (cfg.num_clusters, cfg.dimension))
         iters = ctypes.c_int(0)
-        given = 0
+        init = _ffi.IVF_INIT_KMEANSPP if cfg.init == "kmeans++" else _ffi.IVF_INIT_RANDOM
         if initial_centroids is not None:
             c0 = _f32_2d(initial_centroids, "initial_centroids")
             if c0.shape != (cfg.num_clusters, cfg.dimension):
                 raise InvalidInput(f"initial centroids must be {cfg.num_clusters} x {cfg.dimension}")
             dc.upload(c0)
-            given = 1
+            init = _ffi.IVF_INIT_GIVEN
         _ffi.call("va_ivf_train", ctx.handle, dx.ptr, x.shape[0], cfg.dimension, cfg.num_clusters,
-                  cfg.max_iterations, ctypes.c_float(cfg.convergence_threshold), cfg.seed, given, dc.ptr,
+                  cfg.max_iterations, ctypes.c_float(cfg.convergence_threshold), cfg.seed, init, dc.ptr,
                   ctypes.byref(iters))
         centroids = dc.download()
         assign = _assign(ctx, centroids, dx.ptr, x.shape[0])
