@@ -30,6 +30,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -40,6 +41,7 @@ if ROOT not in sys.path:
 
 METRIC = "queries/sec at N=10M d=768 k=10 (1/2/4/8 B200); % tensor-pipe / HBM roofline"
 QUERY_ROW0 = 1 << 31
+PARITY_QUERIES = 100
 
 
 def parse_args():
@@ -54,6 +56,8 @@ def parse_args():
     p.add_argument("--k", type=int, default=10)
     p.add_argument("--precision", choices=["bf16", "tf32", "fp32"], default="bf16")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the oracle parity check of sampled queries")
+    p.add_argument("--parity-queries", type=int, default=PARITY_QUERIES)
     p.add_argument("--cpu-rows", type=int, default=1_000_000, help="database rows of the CPU sample")
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--config", choices=["headline"] + sorted(CONFIGS) + ["ivf"], default="headline",
@@ -155,6 +159,198 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------ oracle parity
+# The checker leg (after timing): the search's results for a seeded sample of queries against the
+# CPU oracle's exact answer over the WHOLE database. Rows are streamed from the device in chunks
+# (the inputs the GPU searched); every rank checks its own shard and rank 0 merges.
+PARITY_CHUNK_BYTES = 2 << 30
+
+
+def parity_sample(nq: int, count: int = PARITY_QUERIES) -> np.ndarray:
+    rng = np.random.default_rng(20260)
+    return np.sort(rng.choice(nq, size=min(count, nq), replace=False))
+
+
+def download_rows(ctx, dev_ptr: int, r0: int, r1: int, row_elems: int, dtype) -> np.ndarray:
+    from vectoraccelerate_b200 import _ffi
+    out = np.empty((r1 - r0, row_elems), dtype)
+    isz = np.dtype(dtype).itemsize
+    _ffi.call("va_buffer_download", ctx.handle, out.ctypes.data_as(ctypes.c_void_p),
+              ctypes.c_void_p(dev_ptr + r0 * row_elems * isz), ctypes.c_size_t(out.nbytes))
+    ctx.synchronize()
+    return out
+
+
+def merge_best(vals_a, ids_a, vals_b, ids_b, k: int, larger: bool):
+    """Per row, the k best of two candidate lists by (value, id) (value descending when larger)."""
+    v = np.concatenate([vals_a, vals_b], axis=1)
+    i = np.concatenate([ids_a, ids_b], axis=1).astype(np.uint32)
+    invalid = i == 0xFFFFFFFF
+    key = np.where(invalid, np.inf, -v.astype(np.float64) if larger else v.astype(np.float64))
+    order = np.lexsort((i.astype(np.int64), key), axis=1)[:, :k]
+    return np.take_along_axis(v, order, 1), np.take_along_axis(i, order, 1)
+
+
+def shard_truth(kind, ctx, db, q, k, metric, row0, n_local, dim, threads, gpu_ids, candidates=0, sq=None):
+    """Oracle truth over this rank's rows [row0, row0 + n_local) (global ids), and the oracle's exact
+    value of every GPU id that falls in the shard (NaN elsewhere)."""
+    from oracle import oracle
+    P = q.shape[0]
+    larger = metric == 2 and kind == "float"
+    pad = -np.inf if larger else np.inf
+    tv = np.full((P, k), pad, np.float32)
+    ti = np.full((P, k), 0xFFFFFFFF, np.uint32)
+    gtrue = np.full(gpu_ids.shape, np.nan, np.float32)
+    ptr = db.rows_ptr()
+    if kind == "binary":
+        row_elems, dt = dim // 32, np.uint32
+    elif kind == "float" and db.dtype == 1:
+        row_elems, dt = dim, np.uint16
+    else:
+        row_elems, dt = dim, np.float32
+    chunk = max(1, PARITY_CHUNK_BYTES // (row_elems * np.dtype(dt).itemsize))
+    cand_v = cand_i = None
+    for r0 in range(0, n_local, chunk):
+        r1 = min(n_local, r0 + chunk)
+        x = download_rows(ctx, ptr, r0, r1, row_elems, dt)
+        g0 = row0 + r0
+        if kind == "float":
+            ids, vals = oracle.knn(q, x, k, metric=metric, threads=threads, db_bf16=dt == np.uint16)
+        elif kind == "binary":
+            ids, d = oracle.hamming_knn(q, x, k, threads=threads)
+            vals = d.astype(np.float32)
+        else:
+            qc = oracle.sq_perdim_quantize(q, *sq)
+            xc = oracle.sq_perdim_quantize(x, *sq)
+            _, _, cids, cd = oracle.int8_knn(qc, q, xc, x, candidates, 1, threads=threads)
+            cvals = np.where(cd < 0, np.inf, cd).astype(np.float32)
+            cids = np.where(cids == 0xFFFFFFFF, cids, cids + np.uint32(g0))
+            cand_v, cand_i = (cvals, cids) if cand_v is None else merge_best(cand_v, cand_i, cvals, cids,
+                                                                            candidates, False)
+            ids, vals = None, None
+        if ids is not None:
+            ids = np.where(ids == 0xFFFFFFFF, ids, ids + np.uint32(g0))
+            tv, ti = merge_best(tv, ti, vals, ids, k, larger)
+        # exact values of the GPU's ids in this chunk
+        inside = (gpu_ids >= g0) & (gpu_ids < row0 + r1) & (gpu_ids != 0xFFFFFFFF)
+        if inside.any():
+            local = np.where(inside, gpu_ids - np.uint32(g0), 0xFFFFFFFF).astype(np.uint32)
+            if kind == "binary":
+                for p, j in zip(*np.nonzero(inside)):
+                    gtrue[p, j] = float(oracle.hamming_matrix(q[p:p + 1], x[local[p, j]:local[p, j] + 1])[0, 0])
+            else:
+                m = 2 if larger else (metric if kind == "float" else 0)
+                rids, rvals = oracle.rerank(q, x, local, local.shape[1], metric=m, threads=threads,
+                                            db_bf16=dt == np.uint16)
+                for p in range(P):
+                    pos = {int(a): v for a, v in zip(rids[p], rvals[p]) if int(a) != 0xFFFFFFFF}
+                    for j in range(local.shape[1]):
+                        if inside[p, j]:
+                            gtrue[p, j] = pos[int(local[p, j])]
+    if kind == "int8":
+        # the int8 truth of this shard is its candidate list; reranked after the global merge
+        return cand_v, cand_i, gtrue
+    return tv, ti, gtrue
+
+
+def int8_rerank_global(ctx, db, q, k, row0, n_local, dim, threads, cand_i):
+    """Exact fp32-row rerank values of the global candidates that live in this shard (NaN elsewhere)."""
+    from oracle import oracle
+    vals = np.full(cand_i.shape, np.nan, np.float32)
+    chunk = max(1, PARITY_CHUNK_BYTES // (dim * 4))
+    ptr = db.rows_ptr()
+    for r0 in range(0, n_local, chunk):
+        r1 = min(n_local, r0 + chunk)
+        g0 = row0 + r0
+        inside = (cand_i >= g0) & (cand_i < row0 + r1) & (cand_i != 0xFFFFFFFF)
+        if not inside.any():
+            continue
+        x = download_rows(ctx, ptr, r0, r1, dim, np.float32)
+        local = np.where(inside, cand_i - np.uint32(g0), 0xFFFFFFFF).astype(np.uint32)
+        rids, rvals = oracle.rerank(q, x, local, local.shape[1], metric=0, threads=threads)
+        for p in range(q.shape[0]):
+            pos = {int(a): v for a, v in zip(rids[p], rvals[p]) if int(a) != 0xFFFFFFFF}
+            for j in range(local.shape[1]):
+                if inside[p, j]:
+                    vals[p, j] = pos[int(local[p, j])]
+    return vals
+
+
+def all_gather_host(arr: np.ndarray, world: int):
+    """Every rank's copy of a host array, in rank order (on every rank)."""
+    if world == 1:
+        return [arr]
+    import torch
+    import torch.distributed as dist
+    t = torch.from_numpy(np.ascontiguousarray(arr).view(np.uint8).copy()).cuda()
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.cpu().numpy().view(arr.dtype).reshape(arr.shape) for o in out]
+
+
+def oracle_sq_params(ctx, db, n_local, dim, world):
+    """Per-dimension int8 parameters over the WHOLE database, computed on the host from the device
+    rows (min / max per shard, combined over ranks), in the oracle's float32 formula
+    (va_oracle.cpp orc_sq_perdim_params: scale = max((max - min) / 255, 1e-8))."""
+    mn = np.full(dim, np.inf, np.float32)
+    mx = np.full(dim, -np.inf, np.float32)
+    chunk = max(1, PARITY_CHUNK_BYTES // (dim * 4))
+    ptr = db.rows_ptr()
+    for r0 in range(0, n_local, chunk):
+        x = download_rows(ctx, ptr, r0, min(n_local, r0 + chunk), dim, np.float32)
+        mn = np.minimum(mn, x.min(axis=0))
+        mx = np.maximum(mx, x.max(axis=0))
+    mn = np.min(np.stack(all_gather_host(mn, world)), axis=0)
+    mx = np.max(np.stack(all_gather_host(mx, world)), axis=0)
+    return mn, np.maximum((mx - mn) / np.float32(255.0), np.float32(1e-8)).astype(np.float32)
+
+
+def oracle_parity(kind, ctx, db, queries_host, sel, final_vals, final_ids, k, metric, row0, n_local, n_total, dim,
+                  world, candidates=0, sq=None):
+    """Parity of the sampled queries' final results against the oracle over all ranks' rows."""
+    t0 = time.perf_counter()
+    threads = max(1, (os.cpu_count() or 1) // world)
+    q = np.ascontiguousarray(queries_host[sel])
+    gv = np.ascontiguousarray(final_vals[sel])
+    gi = np.ascontiguousarray(final_ids[sel]).view(np.uint32)
+    larger = metric == 2 and kind == "float"
+    tv, ti, gtrue = shard_truth(kind, ctx, db, q, k, metric, row0, n_local, dim, threads, gi, candidates, sq)
+    tvs, tis, gts = all_gather_host(tv, world), all_gather_host(ti, world), all_gather_host(gtrue, world)
+    if kind == "int8":
+        # global integer candidates, then their exact rerank on every shard
+        cv, ci = tvs[0], tis[0]
+        for a, b in zip(tvs[1:], tis[1:]):
+            cv, ci = merge_best(cv, ci, a, b, candidates, False)
+        if world > 1:
+            import torch
+            import torch.distributed as dist
+            t = torch.from_numpy(ci.view(np.int32).copy()).cuda()
+            dist.broadcast(t, 0)
+            ci = t.cpu().numpy().view(np.uint32)
+        rv = int8_rerank_global(ctx, db, q, k, row0, n_local, dim, threads, ci)
+        rvs = all_gather_host(rv, world)
+        rv = np.where(np.isnan(rvs[0]), np.nan, rvs[0])
+        for a in rvs[1:]:
+            rv = np.where(np.isnan(rv), a, rv)
+        rv = np.where(ci == 0xFFFFFFFF, np.inf, rv)
+        order = np.lexsort((ci.astype(np.int64), rv.astype(np.float64)), axis=1)[:, :k]
+        tv, ti = np.take_along_axis(rv, order, 1).astype(np.float32), np.take_along_axis(ci, order, 1)
+    else:
+        tv, ti = tvs[0], tis[0]
+        for a, b in zip(tvs[1:], tis[1:]):
+            tv, ti = merge_best(tv, ti, a, b, k, larger)
+    g = gts[0]
+    for a in gts[1:]:
+        g = np.where(np.isnan(g), a, g)
+    from oracle import parity
+    out = parity.summary(gi, gv, ti, tv, g)
+    out["ok"] = parity.ok(out)
+    out["sample"] = f"{len(sel)} seeded queries (numpy default_rng(20260)) of {queries_host.shape[0]:,}, " \
+                    f"full N={n_total:,}; oracle streamed over the device rows on {threads} threads per rank"
+    out["seconds"] = round(time.perf_counter() - t0, 1)
+    return out
+
+
 # ------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -163,12 +359,11 @@ class ClockSampler:
 
     def __init__(self, gpus: str, enabled: bool = True):
         self.proc = None
-        self.path = os.path.join(ROOT, "_work", f"clocks_{os.getpid()}.csv")
         if not enabled:
             return
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         try:
-            self.f = open(self.path, "w")
+            self.f = tempfile.NamedTemporaryFile("w", suffix=".csv", delete=False)
+            self.path = self.f.name
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", gpus, "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
@@ -346,6 +541,22 @@ def run_ours(a):
             step_e2e()
         e2e_ms = max(e2e_ms, (time.perf_counter() - t0) * 1e3 / a.steps)
 
+    # ---- certificate counts of one step's local search, and oracle parity of sampled queries
+    step_device(dq.data_ptr())
+    torch.cuda.synchronize()
+    unc, exa = ctypes.c_int64(), ctypes.c_int64()
+    _ffi.call("va_last_search_stats", ctx.handle, ctypes.byref(unc), ctypes.byref(exa))
+    unc_all = all_gather_host(np.array([unc.value, exa.value], np.int64), world)
+    exactness = {"uncertified_first_pass": int(sum(u[0] for u in unc_all)),
+                 "exact_route": int(sum(u[1] for u in unc_all)),
+                 "note": "per step, summed over ranks: queries whose first bf16 pass was not certified exact "
+                         "(they take a wider tensor-core pass) and queries that took the exact SIMT route"}
+    if not a.no_parity:
+        vals_h = final[0].cpu().numpy()
+        ids_h = final[1].cpu().numpy()
+        exactness["parity"] = oracle_parity("float", ctx, db, hq.numpy(), parity_sample(a.nq, a.parity_queries),
+                                            vals_h, ids_h, k, 0, row0, n_local, a.n, a.dim, world)
+
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -373,8 +584,10 @@ def run_ours(a):
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": f"{a.precision} filter + f64 exact rerank",
         "data": "synthetic: TestRNG restatement, N(0,1) database seed 0, queries seed 1 (streams offset 2^31)",
-        "config": dict(workload(a), parallelism=f"row-shard x{world}, NCCL allgather + device merge",
-                       precision=a.precision),
+        "config": workload(a),
+        "parallelism": f"row-shard x{world}, NCCL allgather + device merge",
+        "filter_precision": a.precision,
+        "exactness": exactness,
         "e2e": {"value": a.nq / (e2e_ms * 1e-3), "unit": "queries/s",
                 "h2d_bytes_per_step": world * a.nq * a.dim * 4, "d2h_bytes_per_step": world * a.nq * k * 8},
         "gpu_launches": launches_per_step * a.steps if launches_per_step else None,
@@ -574,6 +787,26 @@ def run_config(a):
     e1.record(stream)
     barrier_sync()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+
+    # ---- certificate counts (float configurations) and oracle parity of sampled queries
+    step()
+    torch.cuda.synchronize()
+    exactness = {}
+    if kind == "float":
+        unc, exa = ctypes.c_int64(), ctypes.c_int64()
+        _ffi.call("va_last_search_stats", ctx.handle, ctypes.byref(unc), ctypes.byref(exa))
+        tot = np.sum(np.stack(all_gather_host(np.array([unc.value, exa.value], np.int64), world)), axis=0)
+        exactness = {"uncertified_first_pass": int(tot[0]), "exact_route": int(tot[1])}
+    if not a.no_parity:
+        vals_h = final[0].cpu().numpy()
+        ids_h = final[1].cpu().numpy()
+        if kind == "binary":
+            vals_h = vals_h.view(np.uint32).astype(np.float32)
+        sq = oracle_sq_params(ctx, db, n_local, dim, world) if kind == "int8" else None
+        exactness["parity"] = oracle_parity(kind, ctx, db, hq.numpy().view(np.uint32) if kind == "binary"
+                                            else hq.numpy(), parity_sample(nq, a.parity_queries), vals_h, ids_h,
+                                            k, metric, row0, n_local, n_total, dim, world,
+                                            candidates=c.get("candidates", 0), sq=sq)
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -614,8 +847,9 @@ def run_config(a):
                   "binary": "u1 codes (popcount / s8 0-1 tensor-core contraction)"}[kind],
         "data": "synthetic: TestRNG restatement on the device", "config": {
             "workload": c["desc"], "config": a.config, "N": n_total, "d": dim, "Q": nq, "k": k,
-            "parallelism": f"row-shard x{world}, NCCL allgather + device merge",
             "l2_policy": "inputs larger than L2, no flush"},
+        "parallelism": f"row-shard x{world}, NCCL allgather + device merge",
+        "exactness": exactness,
         "latency_ms": {"p50": p50, "p99": p99},
         "e2e": {"value": nq / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": world * in_bytes,
                 "d2h_bytes_per_step": world * nq * k * 8},

@@ -200,12 +200,21 @@ int va_db_compact(va_context* ctx, va_database* db, const uint8_t* keep, int64_t
  * (Kernels/Metal4/FusedL2TopKKernel.swift:367-427) and the batch flat search
  * AcceleratedVectorIndex.searchBatchGPU (Index/AcceleratedVectorIndex.swift:1278-1374), extended
  * to cosine and inner product. rerank = candidate-pool factor of the reduced-precision pass
- * (pool = rerank * k; 0 = automatic: k + max(k/4, 22), widened to 3k for bf16). The call is
- * stream-ordered, except that a pool wider than 128 candidates reads back (and waits for) the
- * count of queries whose pool could not be proven exact, which then take the FP32 route. A
- * context serves one host thread at a time (its scratch buffers are shared by its calls). */
+ * (pool = rerank * k; 0 = automatic: k + max(k/4, 22), widened to 3k for bf16).
+ * Exactness: the reduced-precision keys only choose a candidate pool, which is reranked exactly;
+ * a per-query certificate (a rigorous bound of the keys' rounding error against the gap between
+ * the k-th exact distance and the pool's last key) proves that no row outside the pool can enter
+ * the top k. Queries that fail it take a second tensor-core pass with a 4x wider pool, and what
+ * that cannot certify takes the exact SIMT route, so every result is the exact top k.
+ * The tensor-core route reads back the count of uncertified queries, so the call waits for the
+ * stream once (twice when a second pass runs). A context serves one host thread at a time (its
+ * scratch buffers are shared by its calls). */
 int va_knn_search(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int metric,
                   int precision, int rerank, float* out_vals, uint32_t* out_ids);
+/* Counts of the last va_knn_search (or va_knn_search_noalloc) on this context: queries whose first
+ * tensor-core pass was not certified exact, and queries that took the exact SIMT route (all of
+ * them on the FP32 route). No reference counterpart (the reference's fused kernel is fp32). */
+int va_last_search_stats(va_context* ctx, int64_t* uncertified, int64_t* exact);
 /* Same, with HOST query and result buffers: copies in, searches, copies out and waits (bounded).
  * This is the whole reference call (findNearestNeighbors, FusedL2TopKKernel.swift:439-529). */
 int va_knn_search_host(va_context* ctx, const va_database* db, const float* queries_host, int64_t nq, int k,
@@ -219,14 +228,21 @@ int va_knn_search_host(va_context* ctx, const va_database* db, const float* quer
  * allocator, and latency-bound paths that cannot take an allocation's implicit synchronisation.
  * Inputs, outputs and the database are the caller's, as for va_knn_search; the search's scratch
  * lives in one fixed device array of VA_NOALLOC_SCRATCH_BYTES that every GPU loading this
- * library holds until exit. Limits: the tensor-core route only (precision AUTO, BF16 or TF32);
- * batches whose scratch exceeds the array are rejected with VA_ERR_INVALID_ARG naming the bytes
- * needed (up to 256 queries fit at any dimension <= VA_MAX_DIM with the default pool); the
- * database must already hold the operand the metric/precision needs (bf16 for L2/IP is built by
- * va_db_create; others by a first va_knn_search), else VA_ERR_UNSUPPORTED. The first call on a
- * device looks up the array's device address (make it before any stream capture). Every call
- * shares the array, so calls that overlap on the GPU (other streams or contexts of the same
- * device) race; serialise them. */
+ * library holds until exit. It resolves AUTO exactly as va_knn_search does and returns the same
+ * exact results (certificate included; uncertified queries take the exact SIMT route inside the
+ * same array). Limits: the tensor-core route only, k <= 128; AUTO resolving to the FP32 route
+ * (d <= 16 with fp32 rows) or k > 128 is rejected with VA_ERR_UNSUPPORTED. The candidate lists
+ * take the route's pool (at most 128 entries) and are halved, never below k, while the batch does
+ * not fit the array (results stay exact: the certificate sends what a thinner pool cannot prove
+ * to the exact route). A batch that fits no list size is rejected with VA_ERR_INVALID_ARG naming
+ * the bytes needed. At d = 768 and millions of rows, 32-entry lists fit about 1,400 queries per
+ * call and 64-entry lists about 500; 128-entry lists (query tiles of 256 on 74 row splits) do not
+ * fit, so k in 65..128 is rejected at that size. The database must
+ * already hold the operand the metric/precision needs (bf16 for L2/IP is built by va_db_create;
+ * others by a first va_knn_search), else VA_ERR_UNSUPPORTED. The first call on a device looks up
+ * the array's device address (make it before any stream capture). Every call shares the array,
+ * so calls that overlap on the GPU (other streams or contexts of the same device) race;
+ * serialise them. The call waits for the stream once (the count of uncertified queries). */
 int va_knn_search_noalloc(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k,
                           int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids);
 

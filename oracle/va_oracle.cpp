@@ -204,6 +204,111 @@ inline float dot_f32(const float* a, const float* b, int d) {
     return s;
 }
 
+// fp64 sum of squared differences / of products with 8 independent partial sums (vectorisable
+// without reassociation flags): the truth accumulation of knn_truth_rows. The summation order
+// differs from a sequential fp64 sum only at the 1e-16 level, before the single rounding to fp32.
+inline double l2sq_f64(const double* a, const double* b, int d) {
+    double acc[8] = {0};
+    int i = 0;
+    for (; i + 8 <= d; i += 8)
+        for (int j = 0; j < 8; ++j) {
+            double t = a[i + j] - b[i + j];
+            acc[j] += t * t;
+        }
+    double s = 0;
+    for (int j = 0; j < 8; ++j) s += acc[j];
+    for (; i < d; ++i) {
+        double t = a[i] - b[i];
+        s += t * t;
+    }
+    return s;
+}
+
+inline double dot_f64(const double* a, const double* b, int d) {
+    double acc[8] = {0};
+    int i = 0;
+    for (; i + 8 <= d; i += 8)
+        for (int j = 0; j < 8; ++j) acc[j] += a[i + j] * b[i + j];
+    double s = 0;
+    for (int j = 0; j < 8; ++j) s += acc[j];
+    for (; i < d; ++i) s += a[i] * b[i];
+    return s;
+}
+
+// Truth-mode k-NN split over row chunks (every host thread busy even for a few queries): each
+// chunk keeps a bounded heap per query over its rows (rows widened to fp64 once per block and
+// reused by every query), then the chunk heaps are merged per query under the same (key, id)
+// order. Same selection and values as the per-query scan of CPUTopK.search.
+void knn_truth_rows(const float* q, int64_t Q, const void* x, int x_dtype, int64_t N, int d, int k, int metric,
+                    int threads, uint32_t* out_ids, float* out_vals) {
+    if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());
+    const float pad = metric == 2 ? -INFINITY : INFINITY;
+    std::vector<double> qd((size_t)Q * d), qn((size_t)Q);
+    for (int64_t i = 0; i < Q; ++i) {
+        double s = 0;
+        for (int j = 0; j < d; ++j) {
+            qd[(size_t)i * d + j] = q[i * d + j];
+            s += (double)q[i * d + j] * q[i * d + j];
+        }
+        qn[(size_t)i] = std::sqrt(s);
+    }
+    const int64_t chunk = std::max<int64_t>(2048, (N + threads * 8 - 1) / ((int64_t)threads * 8));
+    const int64_t nchunks = (N + chunk - 1) / chunk;
+    std::vector<std::vector<TopK>> tops((size_t)nchunks);
+    parallel_for(nchunks, threads, [&](int64_t c) {
+        const int64_t r0 = c * chunk, r1 = std::min(N, r0 + chunk);
+        std::vector<TopK> t;
+        t.reserve((size_t)Q);
+        for (int64_t i = 0; i < Q; ++i) t.emplace_back(k);
+        constexpr int RB = 16;
+        std::vector<double> xd((size_t)RB * d);
+        double xn[RB];
+        for (int64_t b0 = r0; b0 < r1; b0 += RB) {
+            const int nb = (int)std::min<int64_t>(RB, r1 - b0);
+            for (int r = 0; r < nb; ++r) {
+                double s = 0;
+                for (int j = 0; j < d; ++j) {
+                    const double v = load_x(x, x_dtype, (b0 + r) * d + j);
+                    xd[(size_t)r * d + j] = v;
+                    s += v * v;
+                }
+                xn[r] = std::sqrt(s);
+            }
+            for (int64_t i = 0; i < Q; ++i) {
+                const double* qq = qd.data() + (size_t)i * d;
+                for (int r = 0; r < nb; ++r) {
+                    const double* xx = xd.data() + (size_t)r * d;
+                    float val;
+                    if (metric == 0) {
+                        val = (float)l2sq_f64(qq, xx, d);
+                    } else {
+                        const double s = dot_f64(qq, xx, d);
+                        if (metric == 2) {
+                            val = (float)s;
+                        } else {
+                            const double den = qn[(size_t)i] * xn[r];
+                            double sim = den > 0 ? s / den : 0.0;
+                            sim = std::min(1.0, std::max(-1.0, sim));
+                            val = (float)(1.0 - sim);
+                        }
+                    }
+                    uint32_t key = metric == 2 ? ~f2key(val) : f2key(val);
+                    if (std::isnan(val)) key = 0xFFFFFFFFu;
+                    const uint32_t id = (uint32_t)(b0 + r);
+                    if (t[(size_t)i].would_accept(key, id)) t[(size_t)i].push(Cand{key, id, val});
+                }
+            }
+        }
+        tops[(size_t)c] = std::move(t);
+    });
+    parallel_for(Q, threads, [&](int64_t i) {
+        TopK fin(k);
+        for (int64_t c = 0; c < nchunks; ++c)
+            for (const Cand& cd : tops[(size_t)c][(size_t)i].h) fin.push(cd);
+        fin.emit(k, pad, out_ids ? out_ids + i * k : nullptr, out_vals ? out_vals + i * k : nullptr);
+    });
+}
+
 }  // namespace
 
 extern "C" {
@@ -271,6 +376,10 @@ void orc_gen_mixture(float* out, int64_t rows, int dim, uint64_t seed, int64_t r
 // ---------------------------------------------------------------------------------------------
 void orc_knn(const float* q, int64_t Q, const void* x, int x_dtype, int64_t N, int d, int k, int metric,
              int acc, int threads, uint32_t* out_ids, float* out_vals) {
+    if (acc == 1) {
+        knn_truth_rows(q, Q, x, x_dtype, N, d, k, metric, threads, out_ids, out_vals);
+        return;
+    }
     const float pad = metric == 2 ? -INFINITY : INFINITY;
     std::vector<double> xnorm;
     if (metric == 1) {

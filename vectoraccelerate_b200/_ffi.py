@@ -74,6 +74,7 @@ SIGNATURES = {
     "va_knn_search": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_knn_search_host": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_knn_search_noalloc": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
+    "va_last_search_stats": [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
     "va_sq_quantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_dequantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_quantize_int4": [_P, _P, _I64, _F, ctypes.c_int8, _P],

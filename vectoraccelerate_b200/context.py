@@ -107,6 +107,13 @@ class GPUContext:
         _ffi.call("va_last_gpu_time_ms", self.handle, ctypes.byref(ms))
         return float(ms.value)
 
+    def last_search_stats(self) -> tuple[int, int]:
+        """(queries the first tensor-core pass could not certify exact, queries that took the exact
+        route) of the last fused search on this context."""
+        u, e = ctypes.c_int64(), ctypes.c_int64()
+        _ffi.call("va_last_search_stats", self.handle, ctypes.byref(u), ctypes.byref(e))
+        return int(u.value), int(e.value)
+
     def get_buffer(self, size: int, dtype=np.float32, shape=None) -> DeviceBuffer:
         """getBuffer(size:) -- an uninitialised device buffer of ``size`` bytes."""
         return DeviceBuffer(self, size, dtype, shape)

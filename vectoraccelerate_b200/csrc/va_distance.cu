@@ -60,14 +60,19 @@ __global__ void k_cos_pairs(const float* __restrict__ a, const float* __restrict
     }
 }
 
+// Element of a row array: fp32, or bf16 bit patterns widened exactly.
+__device__ __forceinline__ float ld_elem(const float* x, int64_t i) { return x[i]; }
+__device__ __forceinline__ float ld_elem(const uint16_t* x, int64_t i) { return __uint_as_float((uint32_t)x[i] << 16); }
+
 // Row norms |v| for the cosine matrix.
-__global__ void k_row_norms(const float* __restrict__ x, int64_t rows, int dim, float* __restrict__ out) {
+template <class XT>
+__global__ void k_row_norms(const XT* __restrict__ x, int64_t rows, int dim, float* __restrict__ out) {
     int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (r >= rows) return;
     float s = 0.f;
     for (int j = lane; j < dim; j += 32) {
-        float v = x[r * dim + j];
+        float v = ld_elem(x, r * dim + j);
         s = fmaf(v, v, s);
     }
     s = warp_sum(s);
@@ -75,11 +80,11 @@ __global__ void k_row_norms(const float* __restrict__ x, int64_t rows, int dim, 
 }
 
 // Tiled all-pairs matrix: 64 x 64 output tile per block, 256 threads, 4 x 4 outputs each,
-// 32-wide dimension slices staged transposed in shared memory.
+// 32-wide dimension slices staged transposed in shared memory. Rows are fp32 or bf16 (XT).
 constexpr int TM = 64, TN = 64, TK = 32;
 
-template <int OP>  // 0 = squared L2 (direct form), 1 = dot
-__global__ void __launch_bounds__(256) k_matrix(const float* __restrict__ q, int64_t nq, const float* __restrict__ x,
+template <int OP, class XT>  // OP 0 = squared L2 (direct form), 1 = dot
+__global__ void __launch_bounds__(256) k_matrix(const float* __restrict__ q, int64_t nq, const XT* __restrict__ x,
                                                 int64_t nx, int dim, int metric, int flag,
                                                 const float* __restrict__ qn, const float* __restrict__ xn,
                                                 float* __restrict__ out, int64_t out_stride) {
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(256) k_matrix(const float* __restrict__ q, int
             int gc = k0 + c;
             sq[c][r] = (gr < nq && gc < dim) ? q[gr * dim + gc] : 0.f;
             int64_t hr = x0 + r;
-            sx[c][r] = (hr < nx && gc < dim) ? x[hr * dim + gc] : 0.f;
+            sx[c][r] = (hr < nx && gc < dim) ? ld_elem(x, hr * dim + gc) : 0.f;
         }
         __syncthreads();
 #pragma unroll 8
@@ -174,23 +179,39 @@ int va_cosine_pairs(va_context* ctx, const float* a, const float* b, int64_t pai
 }  // extern "C"
 
 // Matrix with caller-provided norm scratch (nq + nx floats; used for cosine only), so internal
-// callers can keep the context workspace for their own buffers.
-int va_distance_matrix_impl(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
-                            int metric, int flag, float* out, int64_t out_stride, float* norm_scratch) {
+// callers can keep the context workspace for their own buffers. x_dtype: VA_DTYPE_F32 rows or
+// VA_DTYPE_BF16 rows (widened exactly).
+template <class XT>
+int distance_matrix_t(va_context* ctx, const float* q, int64_t nq, const XT* x, int64_t nx, int dim, int metric,
+                      int flag, float* out, int64_t out_stride, float* norm_scratch) {
     float *qn = nullptr, *xn = nullptr;
     if (metric == VA_METRIC_COSINE) {
         qn = norm_scratch;
         xn = qn + nq;
-        k_row_norms<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, ctx->stream>>>(q, nq, dim, qn);
-        k_row_norms<<<(unsigned)((nx * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, nx, dim, xn);
+        k_row_norms<float><<<(unsigned)((nq * 32 + 255) / 256), 256, 0, ctx->stream>>>(q, nq, dim, qn);
+        k_row_norms<XT><<<(unsigned)((nx * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, nx, dim, xn);
         VA_TRY(va_check_launch("k_row_norms"));
     }
     dim3 grid((unsigned)((nx + TN - 1) / TN), (unsigned)((nq + TM - 1) / TM));
     if (metric == VA_METRIC_L2SQ)
-        k_matrix<0><<<grid, 256, 0, ctx->stream>>>(q, nq, x, nx, dim, metric, flag, qn, xn, out, out_stride);
+        k_matrix<0, XT><<<grid, 256, 0, ctx->stream>>>(q, nq, x, nx, dim, metric, flag, qn, xn, out, out_stride);
     else
-        k_matrix<1><<<grid, 256, 0, ctx->stream>>>(q, nq, x, nx, dim, metric, flag, qn, xn, out, out_stride);
+        k_matrix<1, XT><<<grid, 256, 0, ctx->stream>>>(q, nq, x, nx, dim, metric, flag, qn, xn, out, out_stride);
     return va_check_launch("k_matrix");
+}
+
+int va_distance_matrix_rows(va_context* ctx, const float* q, int64_t nq, const void* x, int x_dtype, int64_t nx,
+                            int dim, int metric, int flag, float* out, int64_t out_stride, float* norm_scratch) {
+    if (x_dtype == VA_DTYPE_BF16)
+        return distance_matrix_t<uint16_t>(ctx, q, nq, (const uint16_t*)x, nx, dim, metric, flag, out, out_stride,
+                                           norm_scratch);
+    return distance_matrix_t<float>(ctx, q, nq, (const float*)x, nx, dim, metric, flag, out, out_stride,
+                                    norm_scratch);
+}
+
+int va_distance_matrix_impl(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
+                            int metric, int flag, float* out, int64_t out_stride, float* norm_scratch) {
+    return distance_matrix_t<float>(ctx, q, nq, x, nx, dim, metric, flag, out, out_stride, norm_scratch);
 }
 
 extern "C" {

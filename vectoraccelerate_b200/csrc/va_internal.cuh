@@ -62,6 +62,10 @@ struct va_context {
     // queries and results of the exact fallback, the Hamming merge output).
     void* aux = nullptr;
     size_t aux_bytes = 0;
+    // Counts of the last va_knn_search: queries the first tensor-core pass could not certify exact,
+    // and queries that took the exact route.
+    int64_t stat_uncertified = 0;
+    int64_t stat_exact = 0;
 };
 
 // Device staging buffer of at least `bytes` for host-buffer calls.
@@ -104,7 +108,20 @@ struct va_database {
     int64_t stage_rows = 0;      // rows per chunk (0: not chunked)
     int64_t chunk_request = 0;   // rows per chunk set by the caller (0: automatic)
     int64_t cap = 0;             // rows allocated in every per-row array (0: exactly n)
+    // Exactness certificate of the reduced-precision filter: maxima over all rows ever held, as
+    // float bit patterns (non-negative floats order like their bits, so atomicMax applies):
+    // cert[0] = max |x|, cert[1 + kind] = max |operand - exact operand-space row| of operand kind
+    // `kind` (VA_CERT_*). Maxima only grow (a compaction keeps them: still valid upper bounds).
+    uint32_t* cert = nullptr;
+    unsigned cert_ready = 0;     // bit kind set once cert[1 + kind] covers every row
 };
+
+// Operand kinds of the certificate (which reduced-precision copy of a row the filter reads).
+#define VA_CERT_BF16 0     // bf16(x)
+#define VA_CERT_BF16_COS 1 // bf16(x / |x|)
+#define VA_CERT_TF32 2     // x read as tf32 by the tensor core
+#define VA_CERT_TF32_COS 3 // (x / |x|) read as tf32
+#define VA_CERT_WORDS 8
 
 #define VA_DB_FLOAT 0
 #define VA_DB_INT8 1
@@ -265,6 +282,39 @@ __device__ int block_select_radix(int64_t n, int want, Get get, uint64_t* out, S
     }
     __syncthreads();
     return want;
+}
+
+// bf16 round to nearest even (NaN kept quiet), as the tensor-core operands are built.
+__device__ __forceinline__ uint16_t f2bf_rn(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+__device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// Bound of |tf32(v) - v| whatever the tensor core's fp32 -> tf32 conversion does (truncation or
+// rounding of the low 13 mantissa bits, flushing of subnormals): one tf32 unit in the last place,
+// or |v| itself below the normal range.
+__device__ __forceinline__ double tf32_err_bound(float v) {
+    const uint32_t u = __float_as_uint(v) & 0x7FFFFFFFu;
+    if (u < 0x00800000u) return (double)__uint_as_float(u);
+    if ((u & 0x1FFFu) == 0) return 0.0;  // exactly representable (bf16 values among them)
+    return ldexp(1.0, (int)(u >> 23) - 127 - 10);
+}
+
+// One element of a certificate operand: t = the exact operand-space value (v, or v * scale for
+// the unit-norm cosine operands, scale = 1/|x| in fp64) and a bound of |operand - t|, where the
+// operand is what the filter's tensor core multiplies (bf16 built by f2bf_rn from the fp32 value,
+// or the fp32 value read as tf32).
+__device__ __forceinline__ void cert_elem(float v, double scale, int kind, double& t, double& err) {
+    const bool cos = kind == VA_CERT_BF16_COS || kind == VA_CERT_TF32_COS;
+    t = cos ? (double)v * scale : (double)v;
+    const float vf = cos ? (float)t : v;  // the fp32 value the operand is made from
+    if (kind == VA_CERT_BF16 || kind == VA_CERT_BF16_COS)
+        err = fabs((double)bf2f(f2bf_rn(vf)) - t);
+    else
+        err = fabs((double)vf - t) + tf32_err_bound(vf);
 }
 
 // Bounded mbarrier / flag waits: the limit is measured on the global nanosecond timer.

@@ -25,8 +25,8 @@
 #include "va_internal.cuh"
 #include "va_tc.cuh"
 
-int va_distance_matrix_impl(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim,
-                            int metric, int flag, float* out, int64_t out_stride, float* norm_scratch);
+int va_distance_matrix_rows(va_context* ctx, const float* q, int64_t nq, const void* x, int x_dtype, int64_t nx,
+                            int dim, int metric, int flag, float* out, int64_t out_stride, float* norm_scratch);
 
 extern "C" int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* ids, int nlists,
                                        int64_t list_stride, int len, int64_t nq, int k, int mode, float* out_vals,
@@ -47,18 +47,13 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
-__device__ __forceinline__ uint16_t f2bf(float f) {
-    uint32_t u = __float_as_uint(f);
-    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40);
-    u += 0x7FFFu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
-}
 
 // Filter row biases: norms2[r] = |x_r|^2 (fp64 accumulation rounded once) and zbias[r] = 0 for
 // real rows; both +inf for the pad rows up to n_pad so padded tile columns never pass the
-// filter. One warp per row.
+// filter. cert (optional) collects max |x_r| (rounded up) for the exactness certificate. One warp
+// per row.
 __global__ void k_row_bias(const void* rows, int dtype, int64_t n, int64_t n_pad, int dim, float* norms2,
-                           float* zbias) {
+                           float* zbias, uint32_t* cert) {
     int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (r >= n_pad) return;
@@ -72,7 +67,35 @@ __global__ void k_row_bias(const void* rows, int dtype, int64_t n, int64_t n_pad
     if (lane == 0) {
         norms2[r] = r < n ? (float)s : INFINITY;
         zbias[r] = r < n ? 0.f : INFINITY;
+        if (cert && r < n) atomicMax(cert, __float_as_uint(__double2float_ru(sqrt(s))));
     }
+}
+
+// Certificate input of one operand kind: max over rows of |operand row - exact operand-space row|
+// (rounded up), into cert[1 + kind]. Unit-norm kinds scale by 1/|x| in fp64 as k_operand does;
+// zero rows stay zero (no error). One warp per row.
+__global__ void k_operand_err(const void* rows, int dtype, int64_t n, int dim, int kind, uint32_t* cert) {
+    int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    double scale = 1.0;
+    if (kind == VA_CERT_BF16_COS || kind == VA_CERT_TF32_COS) {
+        double s = 0;
+        for (int j = lane; j < dim; j += 32) {
+            double v = load_row(rows, dtype, r * dim + j);
+            s += v * v;
+        }
+        s = warp_sum_d(s);
+        scale = s > 0 ? 1.0 / sqrt(s) : 0.0;
+    }
+    double e2 = 0;
+    for (int j = lane; j < dim; j += 32) {
+        double t, err;
+        va::cert_elem(load_row(rows, dtype, r * dim + j), scale, kind, t, err);
+        e2 += err * err;
+    }
+    e2 = warp_sum_d(e2);
+    if (lane == 0) atomicMax(cert + 1 + kind, __float_as_uint(__double2float_ru(sqrt(e2) * (1.0 + 1e-12))));
 }
 
 // Padded tensor-core operand of rows [0, n_valid) of src (rows beyond n_valid up to n_out are
@@ -99,7 +122,7 @@ __global__ void k_operand(const void* src, int dtype, int64_t n_valid, int64_t n
         float v = 0.f;
         if (r < n_valid && j < dim) v = (float)(load_row(src, dtype, r * dim + j) * scale);
         if constexpr (sizeof(OUT) == 2)
-            o[j] = f2bf(v);
+            o[j] = va::f2bf_rn(v);
         else
             o[j] = v;
     }
@@ -110,13 +133,60 @@ __global__ void k_operand(const void* src, int dtype, int64_t n_valid, int64_t n
 constexpr int MR_THREADS = 256;
 constexpr int MR_POOL = 1024;  // candidates kept in shared memory after the bound test
 
+// Exactness certificate of one reduced-precision pass (see k_merge_rerank).
+struct CertArgs {
+    int on;                // 0: no certificate (exact integer keys)
+    int kind;              // VA_CERT_* operand kind the filter multiplied
+    int dpad;              // accumulated products per key (padded dimension)
+    const uint32_t* cert;  // database maxima: [0] max |x|, [1 + kind] max operand error (float bits)
+};
+
+// The certificate. The filter orders rows by an approximate key K(y); the exact key is
+//   D(y) = |y|^2 - 2 q.y (L2: distance - |q|^2),  -q.y (IP),  -cos(q, y) (cosine),
+// which orders rows exactly as the reference's distance does. With a = q (or q/|q|), b = y (or
+// y/|y|) and the tensor core's operands a~ = a + da, b~ = b + db:
+//   a~.b~ - a.b = a~.db + da.b, so |a~.b~ - a.b| <= |a~| max|db| + |da| max|b|   (Cauchy-Schwarz)
+//   |fp32 accumulation - a~.b~| <= g |a~| (max|b| + max|db|), g = dpad * 2^-22 (any summation
+//       order, truncating adders: products of bf16 / tf32 values are exact in fp32)
+//   plus the rounding of the key's fma and of the fp32 |y|^2 bias (2^-24 relative each).
+// |da| and |a| come from this query; max|b| and max|db| are maxima over every row of the
+// database (k_row_bias, k_operand_err). So |K(y) - D(y)| <= eps for every row y, including the
+// rows the filter dropped. Every dropped row has K(y) >= T, the pool's largest approximate key
+// (the pool is the exact top pool by (K, id): a list only drops keys at or above its last one,
+// and the shared bound never cuts into the pool), hence D(y) >= T - eps. If the k-th exact key
+// D_k (from the fp64 rerank, rounded up) satisfies D_k + eps < T, no dropped row can reach the
+// top k: the result is the exact top k. Otherwise the query goes to the fail list.
+__device__ __forceinline__ bool certify(const CertArgs& ca, int metric, float vk, double qn2, double a_norm,
+                                        double a_err, float T) {
+    const double u24 = 5.9604644775390625e-08, u22 = 2.384185791015625e-07;
+    double dk;  // upper bound of the k-th exact key
+    if (metric == VA_METRIC_L2SQ)
+        dk = (double)vk * (1.0 + 4.0 * u24) - qn2 * (1.0 - 1e-12);
+    else if (metric == VA_METRIC_IP)
+        dk = -(double)vk + fabs((double)vk) * 4.0 * u24 + 1e-30;
+    else
+        dk = (double)vk - 1.0 + 4.0 * u24;
+    const double mx = (double)__uint_as_float(ca.cert[0]);
+    const double md = (double)__uint_as_float(ca.cert[1 + ca.kind]);
+    const double mb = metric == VA_METRIC_COSINE ? 1.0 : mx;
+    const double A = a_norm + a_err;  // >= |a~|
+    const double g = (double)ca.dpad * u22;
+    double eps = A * md + a_err * mb + g * A * (mb + md);
+    if (metric == VA_METRIC_L2SQ)
+        eps = 2.0 * eps + u24 * (2.0 * A * (mb + md) * (1.0 + g) + mb * mb) + 2.0 * u24 * mb * mb;
+    else
+        eps += u24 * A * (mb + md) * (1.0 + g);
+    eps = eps * (1.0 + 1e-6) + 1e-30;
+    return dk + eps < (double)T;
+}
+
 __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
                                                            const uint32_t* __restrict__ part_ids, int splits,
                                                            int64_t nq_pad, int kp, int pool_n,
                                                            const float* __restrict__ queries,
                                                            const void* __restrict__ rows, int dtype, int dim, int metric,
                                                            int k, uint32_t id_base, const uint32_t* __restrict__ gthr,
-                                                           BoundLevels lv,
+                                                           BoundLevels lv, int prove, CertArgs ca,
                                                            float* __restrict__ out_vals,
                                                            uint32_t* __restrict__ out_ids,
                                                            uint32_t* __restrict__ fail_list,
@@ -128,8 +198,9 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
     uint64_t* pool = ex + kp2;              // [MR_POOL] candidates at or below the shared bound
     float* sq = (float*)(pool + MR_POOL);   // [dim]
     __shared__ va::SelectShared sh;
-    __shared__ double s_qn;
+    __shared__ double s_qn, s_qn2, s_an, s_ae;
     __shared__ int s_cnt;
+    __shared__ unsigned long long s_t;
     const int64_t qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
 
@@ -152,7 +223,10 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         for (int sl = 0; sl < lv.slots[l]; ++sl) m = max(m, gthr[(int64_t)(lv.off[l] + sl) * nq_pad + qi]);
         bound = min(bound, m);
     }
-    if (threadIdx.x == 0) s_cnt = 0;
+    if (threadIdx.x == 0) {
+        s_cnt = 0;
+        s_t = 0;
+    }
     __syncthreads();
     // Lists are sorted by key: one thread walks each split's list and stops at the first key
     // above the bound or the first empty entry, so only the useful prefix is read.
@@ -174,20 +248,19 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         m = va::block_select_radix((int64_t)n_pool, pool_n, [&](int64_t i) -> uint64_t { return pool[i]; }, sel, sh);
     else
         m = va::block_select_radix(n_all, pool_n, get, sel, sh);
-    if (fail_list) {
-        // Pool wider than the lists (kp < pool_n, lists filled without a shared bound): the
-        // selection is the exact top pool_n by (key, id) when every split's list holds all of its
-        // candidates up to the selection's largest composite T, i.e. when no full list ends below
-        // T. Otherwise the query is handed to the exact fallback.
-        __shared__ unsigned long long s_t;
-        if (threadIdx.x == 0) s_t = 0;
-        __syncthreads();
+    // T: the pool's largest composite (~0 when the pool holds padding, i.e. every candidate).
+    {
         unsigned long long t = 0;
-        for (int i = threadIdx.x; i < m; i += blockDim.x)
-            if (sel[i] != ~0ull && sel[i] > t) t = sel[i];
+        for (int i = threadIdx.x; i < m; i += blockDim.x) t = sel[i] > t ? sel[i] : t;
+        if (m < pool_n) t = ~0ull;
         atomicMax(&s_t, t);
-        __syncthreads();
-        const unsigned long long T = s_t;
+    }
+    __syncthreads();
+    const unsigned long long T = s_t;
+    if (prove) {
+        // Pool wider than the lists (kp < pool_n): the selection is the exact top pool_n by
+        // (key, id) when every split's list holds all of its candidates up to T, i.e. when no full
+        // list ends below T. Otherwise the query is handed to the fallback.
         int bad = 0;
         for (int s = threadIdx.x; s < splits; s += blockDim.x) {
             const uint64_t last = get((int64_t)s * kp + kp - 1);
@@ -198,11 +271,29 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
             return;
         }
     }
-    if (metric == VA_METRIC_COSINE && warp == 0) {
+    if (warp == 0 && (metric == VA_METRIC_COSINE || ca.on)) {
         double s = 0;
         for (int j = lane; j < dim; j += 32) s += (double)sq[j] * sq[j];
         s = warp_sum_d(s);
-        if (lane == 0) s_qn = sqrt(s);
+        double an = 0, ae = 0;
+        if (ca.on) {
+            // |a| and a bound of |a~ - a| for this query's operand (same construction as k_operand)
+            const double scale = metric == VA_METRIC_COSINE ? (s > 0 ? 1.0 / sqrt(s) : 0.0) : 1.0;
+            for (int j = lane; j < dim; j += 32) {
+                double t, err;
+                va::cert_elem(sq[j], scale, ca.kind, t, err);
+                an += t * t;
+                ae += err * err;
+            }
+            an = warp_sum_d(an);
+            ae = warp_sum_d(ae);
+        }
+        if (lane == 0) {
+            s_qn2 = s;
+            s_qn = sqrt(s);
+            s_an = sqrt(an) * (1.0 + 1e-12);
+            s_ae = sqrt(ae) * (1.0 + 1e-12);
+        }
     }
     __syncthreads();
     const int mode = metric == VA_METRIC_IP ? 1 : 0;
@@ -269,6 +360,19 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         }
     }
     va::block_bitonic_sort(ex, kp2);
+    if (ca.on && T != ~0ull) {
+        // The pool holds at least pool_n >= k valid candidates here, so ex[k - 1] is the k-th.
+        __shared__ int s_ok;
+        if (threadIdx.x == 0) {
+            const float vk = va::mode_val((uint32_t)(ex[k - 1] >> 32), mode);
+            s_ok = certify(ca, metric, vk, s_qn2, s_an, s_ae, va::key2f((uint32_t)(T >> 32))) ? 1 : 0;
+        }
+        __syncthreads();
+        if (!s_ok) {
+            if (threadIdx.x == 0) fail_list[atomicAdd(fail_cnt, 1u)] = (uint32_t)qi;
+            return;
+        }
+    }
     const float pad = mode ? -INFINITY : INFINITY;
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
         uint64_t comp = i < kp2 ? ex[i] : ~0ull;
@@ -292,7 +396,21 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 int warps_grid(int64_t warps) { return (int)((warps * 32 + 255) / 256); }
 
-// Build (once) the operand a precision/metric needs.
+int cert_kind(int elem, bool cosine) {
+    return elem == 2 ? (cosine ? VA_CERT_BF16_COS : VA_CERT_BF16) : (cosine ? VA_CERT_TF32_COS : VA_CERT_TF32);
+}
+
+// Certificate input of one operand kind over rows [r0, r0 + count): max operand error, into
+// db->cert[1 + kind] (maxima only grow).
+int operand_err(va_context* ctx, va_database* db, int kind, int64_t r0, int64_t count) {
+    if (count <= 0) return VA_OK;
+    const size_t esz = db->dtype == VA_DTYPE_BF16 ? 2 : 4;
+    const void* src = (const uint8_t*)db->rows + (size_t)r0 * db->dim * esz;
+    k_operand_err<<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, db->dim, kind, db->cert);
+    return va_check_launch("k_operand_err");
+}
+
+// Build (once) the operand a precision/metric needs, with its certificate input.
 int ensure_operand(va_context* ctx, va_database* db, int elem, bool cosine, const void** out) {
     const int64_t n = db->n;
     if (elem == 2) {
@@ -302,7 +420,7 @@ int ensure_operand(va_context* ctx, va_database* db, int elem, bool cosine, cons
                 db->op = (uint16_t*)db->rows;
                 db->op_alias = true;
             } else {
-                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)n * db->dpad * 2));
+                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)std::max<int64_t>(n, db->cap) * db->dpad * 2));
                 k_operand<uint16_t><<<warps_grid(n), 256, 0, ctx->stream>>>(db->rows, db->dtype, n, n, db->dim,
                                                                             db->dpad, cosine ? 1 : 0, *slot);
                 VA_TRY(va_check_launch("k_operand<bf16>"));
@@ -316,13 +434,18 @@ int ensure_operand(va_context* ctx, va_database* db, int elem, bool cosine, cons
                 db->op_f32 = (float*)db->rows;
                 db->op_f32_alias = true;
             } else {
-                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)n * db->dpad * 4));
+                VA_CUDA_TRY(cudaMalloc((void**)slot, (size_t)std::max<int64_t>(n, db->cap) * db->dpad * 4));
                 k_operand<float><<<warps_grid(n), 256, 0, ctx->stream>>>(db->rows, db->dtype, n, n, db->dim,
                                                                          db->dpad, cosine ? 1 : 0, *slot);
                 VA_TRY(va_check_launch("k_operand<f32>"));
             }
         }
         *out = *slot;
+    }
+    const int kind = cert_kind(elem, cosine);
+    if (!(db->cert_ready & (1u << kind))) {
+        VA_TRY(operand_err(ctx, db, kind, 0, n));
+        db->cert_ready |= 1u << kind;
     }
     return VA_OK;
 }
@@ -340,7 +463,7 @@ int choose_kp(int k, int rerank) {
 }
 
 // Pool of va_knn_search: as choose_kp up to 128; above it the wanted size itself (the filter then
-// keeps 128-entry lists without a shared bound), up to VA_MAX_SELECT_K; 0 when larger.
+// keeps 64- or 128-entry lists and the merge proves the pool), up to VA_MAX_SELECT_K; 0 when larger.
 int choose_pool(int k, int rerank) {
     const int kp = choose_kp(k, rerank);
     if (kp) return kp;
@@ -348,12 +471,17 @@ int choose_pool(int k, int rerank) {
     return want <= VA_MAX_SELECT_K ? (int)want : 0;
 }
 
+// Pool of the second tensor-core pass over the queries the first pass could not certify: at least
+// four times wider (and at least 128); 0 when no wider pool is supported (exact route next).
+int wider_pool(int pool) {
+    const int p = std::min(std::max(4 * pool, 128), VA_MAX_SELECT_K);
+    return p > pool ? p : 0;
+}
+
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids, int pool_n = 0, uint32_t* fail_list = nullptr,
-                 uint32_t* fail_cnt = nullptr);
-int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, float* out_vals,
-                uint32_t* out_ids);
+                 float* out_vals, uint32_t* out_ids, int pool_n, int prove, const CertArgs& ca,
+                 uint32_t* fail_list, uint32_t* fail_cnt);
 
 __global__ void k_gather_rows(const float* __restrict__ src, int dim, const uint32_t* __restrict__ rows, int64_t n,
                               float* __restrict__ dst) {
@@ -376,27 +504,111 @@ __global__ void k_scatter_results(const float* __restrict__ v, const uint32_t* _
 
 int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8192)); }
 
-// Failed queries of a wide-pool merge (fail_cnt entries of fail_list): exact FP32 search of those
-// queries, results written to their rows. Reads the count back, so the call waits for the stream.
-int fallback_exact(va_context* ctx, va_database* db, const float* queries, int k, int metric,
-                   const uint32_t* fail_list, const uint32_t* fail_cnt, float* gq, float* gv, uint32_t* gi,
-                   float* out_vals, uint32_t* out_ids) {
-    uint32_t nf = 0;
-    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_TRY(va_synchronize(ctx));
-    if (!nf) return VA_OK;
-    k_gather_rows<<<grid_for((int64_t)nf * db->dim), 256, 0, ctx->stream>>>(queries, db->dim, fail_list, nf, gq);
-    VA_TRY(va_check_launch("k_gather_rows"));
-    VA_TRY(search_fp32(ctx, db, gq, nf, k, metric, gv, gi));
-    k_scatter_results<<<grid_for((int64_t)nf * k), 256, 0, ctx->stream>>>(gv, gi, fail_list, nf, k, out_vals, out_ids);
+int gather_queries(va_context* ctx, const float* src, int dim, const uint32_t* list, int64_t n, float* dst) {
+    k_gather_rows<<<grid_for(n * dim), 256, 0, ctx->stream>>>(src, dim, list, n, dst);
+    return va_check_launch("k_gather_rows");
+}
+
+int scatter_results(va_context* ctx, const float* v, const uint32_t* ids, const uint32_t* list, int64_t n, int k,
+                    float* out_v, uint32_t* out_i) {
+    k_scatter_results<<<grid_for(n * k), 256, 0, ctx->stream>>>(v, ids, list, n, k, out_v, out_i);
     return va_check_launch("k_scatter_results");
 }
 
-// pool <= 128: lists of the pool's size sharing a per-query bound. pool > 128: 128-entry lists
-// without a shared bound; the merge selects the pool from their union where that is provably the
-// exact top pool (see k_merge_rerank) and the remaining queries take the exact FP32 route.
-int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
-              int pool, float* out_vals, uint32_t* out_ids) {
+// Count written by a merge (the call waits for the stream: the next passes depend on it).
+int read_count(va_context* ctx, const uint32_t* dcnt, uint32_t* n) {
+    VA_CUDA_TRY(cudaMemcpyAsync(n, dcnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return va_synchronize(ctx);
+}
+
+// Exact route: the reference's chunked two-pass strategy (executeChunkedTwoPass,
+// FusedL2TopKKernel.swift:765-1090) on fp32 SIMT distance tiles of the ORIGINAL rows (fp32 or
+// bf16 widened exactly), per-chunk top-k and a running device merge. Scratch: `ws` of `ws_bytes`
+// when given, else the context workspace.
+int search_exact(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
+                 float* out_vals, uint32_t* out_ids, void* ws = nullptr, size_t ws_bytes = 0) {
+    const int mode = metric == VA_METRIC_IP ? VA_SELECT_MAX : VA_SELECT_MIN;
+    const int flag = metric == VA_METRIC_COSINE ? 1 : 0;
+    VA_REQUIRE((nq + 63) / 64 <= 65535, "numQueries %lld too large for the exact route", (long long)nq);
+    const size_t lists = (size_t)nq * k;
+    int64_t chunk;
+    if (ws) {
+        // mat (nq x chunk) + norms (nq + chunk) + lists (8 B per entry) within ws_bytes
+        const int64_t avail = (int64_t)ws_bytes - (int64_t)lists * 8 - (int64_t)nq * 4 - 512;
+        chunk = avail / (4 * nq + 4);
+        if (chunk < 64)
+            return va_set_error(VA_ERR_INVALID_ARG,
+                                "the exact route for %lld queries needs more than the %zu bytes of scratch available",
+                                (long long)nq, ws_bytes);
+    } else {
+        chunk = std::max<int64_t>(256, (int64_t)(256ll << 20) / (4 * std::max<int64_t>(nq, 1)));
+    }
+    chunk = std::min<int64_t>(chunk, db->n);
+    const size_t mat = (size_t)nq * chunk;
+    const size_t norms = (size_t)nq + chunk;
+    if (!ws) VA_TRY(va_workspace(ctx, (mat + norms) * 4 + lists * 8 + 512, &ws));
+    float* dmat = (float*)ws;
+    float* cv = dmat + mat;
+    uint32_t* ci = (uint32_t*)(cv + lists);
+    float* nscratch = (float*)(ci + lists);
+    const size_t esz = db->dtype == VA_DTYPE_BF16 ? 2 : 4;
+    for (int64_t c0 = 0; c0 < db->n; c0 += chunk) {
+        const int64_t cn = std::min<int64_t>(chunk, db->n - c0);
+        VA_TRY(va_distance_matrix_rows(ctx, queries, nq, (const uint8_t*)db->rows + (size_t)c0 * db->dim * esz,
+                                       db->dtype, cn, db->dim, metric, flag, dmat, cn, nscratch));
+        if (c0 == 0) {
+            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, out_vals, out_ids, k));
+        } else {
+            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, cv, ci, k));
+            VA_TRY(va_topk_merge(ctx, out_vals, out_ids, k, cv, ci, k, (uint32_t)c0, nq, mode, out_vals, out_ids));
+        }
+    }
+    if (db->id_base) {
+        k_add_base<<<std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096)), 256, 0, ctx->stream>>>(
+            out_ids, nq * k, db->id_base);
+        VA_TRY(va_check_launch("k_add_base"));
+    }
+    return VA_OK;
+}
+
+// Filter arguments shared by the tensor-core passes.
+TcFilterArgs filter_args(va_database* db, int metric, int elem, const void* q_op, const void* x_op,
+                         const TcPlan& plan, float* part_keys, uint32_t* part_ids, uint32_t* gthr,
+                         uint32_t* sync_cnt) {
+    TcFilterArgs a = {};
+    a.q_op = q_op;
+    a.x_op = x_op;
+    a.elem_bytes = elem;
+    a.dpad = db->dpad;
+    a.n_rows = db->n;
+    a.row_bias = metric == VA_METRIC_L2SQ ? db->norms2 : db->zbias;
+    a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
+    a.part_keys = part_keys;
+    a.part_ids = part_ids;
+    a.gthr = gthr;          // va_tc_filter resets it before the launch
+    a.sync_cnt = sync_cnt;  // likewise
+    a.sync_words = plan.sync_words;
+    // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
+    a.limit_ms = 2000u;
+    a.levels = plan.levels;
+    return a;
+}
+
+CertArgs cert_args(va_database* db, int elem, int metric) {
+    CertArgs ca;
+    ca.on = 1;
+    ca.kind = cert_kind(elem, metric == VA_METRIC_COSINE);
+    ca.dpad = db->dpad;
+    ca.cert = db->cert;
+    return ca;
+}
+
+// One tensor-core pass over queries[nq]: operand, filter, merge with exact rerank and the
+// certificate. Queries that are not certified exact (and, for pools wider than the lists,
+// queries whose pool is not proven) are appended to fail_list / fail_cnt (indices into
+// `queries`) and get no output rows. `timed`: bracket the filter with the context's events.
+int tc_pass(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem, int pool,
+            float* out_vals, uint32_t* out_ids, uint32_t* fail_list, uint32_t* fail_cnt, bool timed) {
     const bool wide = pool > 128;
     TcPlan plan;
     VA_TRY(va_tc_plan_pool(ctx, nq, db->n, pool, &plan, (int64_t)db->dpad * elem));
@@ -404,7 +616,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = nullptr;
     VA_TRY(ensure_operand(ctx, db, elem, cosine, &x_op));
-    // Scratch: query operand, partial lists, shared per-query bounds.
+    // Scratch: query operand, partial lists, shared per-query bounds, pacing counters.
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
     const size_t bytes = round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.bound_slots * plan.nq_pad * 4 +
@@ -425,106 +637,112 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
         k_operand<float><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
     VA_TRY(va_check_launch("k_operand(queries)"));
-
-    TcFilterArgs a = {};
-    a.q_op = q_op;
-    a.x_op = x_op;
-    a.elem_bytes = elem;
-    a.dpad = db->dpad;
-    a.n_rows = db->n;
-    a.row_bias = metric == VA_METRIC_L2SQ ? db->norms2 : db->zbias;
-    a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
-    a.part_keys = part_keys;
-    a.part_ids = part_ids;
-    a.gthr = gthr;
-    a.sync_cnt = sync_cnt;
-    a.sync_words = plan.sync_words;
-    // A single pipeline wait lasts microseconds; 2 s means the pipeline is stuck.
-    a.limit_ms = 2000u;
-    a.levels = plan.levels;
-    // Wide pools: failure list and the fallback's gathered queries and results, sized before any
-    // kernel writes them.
-    uint32_t* fail_cnt = nullptr;
-    uint32_t* fail_list = nullptr;
-    float *gq = nullptr, *gv = nullptr;
-    uint32_t* gi = nullptr;
-    if (wide) {
-        void* aux;
-        const size_t lb = round_up(4 * (nq + 64), 256), qb = round_up(nq * db->dim * 4, 256),
-                     rb = round_up(nq * k * 4, 256);
-        VA_TRY(va_aux_buffer(ctx, lb + qb + 2 * rb, &aux));
-        fail_cnt = (uint32_t*)aux;
-        fail_list = fail_cnt + 64;
-        gq = (float*)((uint8_t*)aux + lb);
-        gv = (float*)((uint8_t*)gq + qb);
-        gi = (uint32_t*)((uint8_t*)gv + rb);
-        VA_CUDA_TRY(cudaMemsetAsync(fail_cnt, 0, 4, ctx->stream));
-    }
-    const bool prof = ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
-    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
+    const TcFilterArgs a = filter_args(db, metric, elem, q_op, x_op, plan, part_keys, part_ids, gthr, sync_cnt);
+    const bool prof = timed && ctx->prof_ev && ctx->prof_n < ctx->prof_cap;
+    if (timed) VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n] : ctx->ev_k0, ctx->stream));
     VA_TRY(va_tc_filter(ctx, a, plan));
-    VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
-    if (prof)
-        ctx->prof_n++;
-    else
-        ctx->k_recorded = true;
-    if (!wide) return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
-    VA_TRY(merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool,
-                        fail_list, fail_cnt));
-    return fallback_exact(ctx, db, queries, k, metric, fail_list, fail_cnt, gq, gv, gi, out_vals, out_ids);
+    if (timed) {
+        VA_CUDA_TRY(cudaEventRecord(prof ? ctx->prof_ev[2 * ctx->prof_n + 1] : ctx->ev_k1, ctx->stream));
+        if (prof)
+            ctx->prof_n++;
+        else
+            ctx->k_recorded = true;
+    }
+    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids,
+                        wide ? pool : 0, wide ? 1 : 0, cert_args(db, elem, metric), fail_list, fail_cnt);
+}
+
+// Tensor-core search with exactness guaranteed: pass 1 at `pool`; the queries it cannot certify
+// take a second tensor-core pass with a wider pool; what that cannot certify takes the exact
+// route. Each later pass reads back the count of the previous one (the call waits for the stream).
+int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
+              int pool, float* out_vals, uint32_t* out_ids) {
+    // aux (sized before any kernel writes it): counters, two fail lists, gathered queries and
+    // results of the second pass and of the exact route.
+    const size_t cb = 256, lb = round_up(4 * nq, 256), qb = round_up(nq * db->dim * 4, 256),
+                 rb = round_up(nq * k * 4, 256);
+    void* aux;
+    VA_TRY(va_aux_buffer(ctx, cb + 2 * lb + 2 * qb + 4 * rb, &aux));
+    uint8_t* p = (uint8_t*)aux;
+    uint32_t* cnt = (uint32_t*)p;  // [0] pass 1, [32] pass 2
+    uint32_t* list1 = (uint32_t*)(p + cb);
+    uint32_t* list2 = (uint32_t*)(p + cb + lb);
+    float* gq1 = (float*)(p + cb + 2 * lb);
+    float* gq2 = (float*)((uint8_t*)gq1 + qb);
+    float* gv1 = (float*)((uint8_t*)gq2 + qb);
+    uint32_t* gi1 = (uint32_t*)((uint8_t*)gv1 + rb);
+    float* gv2 = (float*)((uint8_t*)gi1 + rb);
+    uint32_t* gi2 = (uint32_t*)((uint8_t*)gv2 + rb);
+    VA_CUDA_TRY(cudaMemsetAsync(cnt, 0, cb, ctx->stream));
+    VA_TRY(tc_pass(ctx, db, queries, nq, k, metric, elem, pool, out_vals, out_ids, list1, cnt, true));
+    uint32_t n1 = 0;
+    VA_TRY(read_count(ctx, cnt, &n1));
+    ctx->stat_uncertified = n1;
+    if (!n1) return VA_OK;
+    VA_TRY(gather_queries(ctx, queries, db->dim, list1, n1, gq1));
+    const int pool2 = wider_pool(pool);
+    if (pool2) {
+        VA_TRY(tc_pass(ctx, db, gq1, n1, k, metric, elem, pool2, gv1, gi1, list2, cnt + 32, false));
+        uint32_t n2 = 0;
+        VA_TRY(read_count(ctx, cnt + 32, &n2));
+        ctx->stat_exact = n2;
+        if (n2) {
+            VA_TRY(gather_queries(ctx, gq1, db->dim, list2, n2, gq2));
+            VA_TRY(search_exact(ctx, db, gq2, n2, k, metric, gv2, gi2));
+            VA_TRY(scatter_results(ctx, gv2, gi2, list2, n2, k, gv1, gi1));
+        }
+    } else {
+        ctx->stat_exact = n1;
+        VA_TRY(search_exact(ctx, db, gq1, n1, k, metric, gv1, gi1));
+    }
+    return scatter_results(ctx, gv1, gi1, list1, n1, k, out_vals, out_ids);
 }
 
 int merge_rerank(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                  const TcPlan& plan, const float* part_keys, const uint32_t* part_ids, const uint32_t* gthr,
-                 float* out_vals, uint32_t* out_ids, int pool_n, uint32_t* fail_list, uint32_t* fail_cnt) {
+                 float* out_vals, uint32_t* out_ids, int pool_n, int prove, const CertArgs& ca,
+                 uint32_t* fail_list, uint32_t* fail_cnt) {
     const int kp2 = va::next_pow2(std::max(plan.kp, pool_n));
     size_t smem = (size_t)kp2 * 16 + (size_t)MR_POOL * 8 + (size_t)db->dim * 4;
     if (smem > 48 * 1024)
         VA_CUDA_TRY(cudaFuncSetAttribute(k_merge_rerank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if ((prove || ca.on) && !(fail_list && fail_cnt))
+        return va_set_error(VA_ERR_INVALID_ARG, "internal: a proving or certifying merge needs a fail list");
     k_merge_rerank<<<(unsigned)nq, MR_THREADS, smem, ctx->stream>>>(part_keys, part_ids, plan.splits, plan.nq_pad,
                                                                     plan.kp, pool_n > 0 ? pool_n : plan.kp, queries,
                                                                     db->rows, db->dtype, db->dim,
                                                                     metric, k, db->id_base, gthr, plan.levels,
-                                                                    out_vals, out_ids,
+                                                                    prove, ca, out_vals, out_ids,
                                                                     fail_list, fail_cnt);
     return va_check_launch("k_merge_rerank");
 }
 
-int search_fp32(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, float* out_vals,
-                uint32_t* out_ids) {
-    if (db->dtype != VA_DTYPE_F32)
-        return va_set_error(VA_ERR_UNSUPPORTED, "precision FP32 needs an fp32 database (this one is bf16)");
-    const int mode = metric == VA_METRIC_IP ? VA_SELECT_MAX : VA_SELECT_MIN;
-    const int flag = metric == VA_METRIC_COSINE ? 1 : 0;
-    int64_t chunk = std::max<int64_t>(256, (int64_t)(256ll << 20) / (4 * std::max<int64_t>(nq, 1)));
-    chunk = std::min<int64_t>(chunk, db->n);
-    const size_t mat = (size_t)nq * chunk;
-    const size_t lists = (size_t)nq * k;
-    const size_t norms = (size_t)nq + chunk;
-    void* ws;
-    VA_TRY(va_workspace(ctx, (mat + norms) * 4 + lists * 8 + 512, &ws));
-    float* dmat = (float*)ws;
-    float* cv = dmat + mat;
-    uint32_t* ci = (uint32_t*)(cv + lists);
-    float* nscratch = (float*)(ci + lists);
-    const float* rows = (const float*)db->rows;
-    for (int64_t c0 = 0; c0 < db->n; c0 += chunk) {
-        const int64_t cn = std::min<int64_t>(chunk, db->n - c0);
-        VA_REQUIRE((nq + 63) / 64 <= 65535, "numQueries %lld too large for the FP32 route", (long long)nq);
-        VA_TRY(va_distance_matrix_impl(ctx, queries, nq, rows + c0 * db->dim, cn, db->dim, metric, flag, dmat, cn,
-                                       nscratch));
-        if (c0 == 0) {
-            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, out_vals, out_ids, k));
-        } else {
-            VA_TRY(va_topk_select(ctx, dmat, nq, cn, cn, k, mode, cv, ci, k));
-            VA_TRY(va_topk_merge(ctx, out_vals, out_ids, k, cv, ci, k, (uint32_t)c0, nq, mode, out_vals, out_ids));
-        }
+// Route of a float search after AUTO: the contraction precision and the candidate pool (pool 0
+// with precision FP32: the exact route).
+int plan_route(const va_database* db, int k, int precision, int rerank, int* prec_out, int* pool_out) {
+    int pool = choose_pool(k, rerank);
+    int prec = precision;
+    // AUTO: bf16 when the pool holds at least 3k candidates. Without a caller's factor, fp32 rows
+    // take a 3k pool (wider than 128 from k = 43 on) to stay on bf16; otherwise (bf16 rows, a thin
+    // caller-set pool) the 4x smaller tf32 error keeps more queries certified in the first pass.
+    // No pool size -> exact route. Rows of at most 16 dimensions (fp32) take the exact route too:
+    // few dimensions give the reduced-precision keys no resolution between close neighbours (for
+    // d = 1 a bf16 key cannot order points 1/N apart), so most queries would fail the
+    // certificate, and the SIMT route is cheap there.
+    if (prec == VA_PREC_AUTO) {
+        if (pool && pool < 3 * k && rerank == 0 && db->dtype == VA_DTYPE_F32 && 3 * k <= VA_MAX_SELECT_K)
+            pool = 3 * k;
+        prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
+        if (db->dim <= 16 && db->dtype == VA_DTYPE_F32) prec = VA_PREC_FP32;
     }
-    if (db->id_base) {
-        k_add_base<<<std::max(1, (int)std::min<int64_t>((nq * k + 255) / 256, 4096)), 256, 0, ctx->stream>>>(
-            out_ids, nq * k, db->id_base);
-        VA_TRY(va_check_launch("k_add_base"));
-    }
+    if (prec != VA_PREC_FP32 && !pool)
+        return va_set_error(VA_ERR_UNSUPPORTED,
+                            "candidate pool %lld of k %d is not supported by the tensor-core route (at most %d); "
+                            "use precision FP32",
+                            (long long)(rerank ? (int64_t)rerank * k : (int64_t)k + std::max(k / 4, 22)), k,
+                            VA_MAX_SELECT_K);
+    *prec_out = prec;
+    *pool_out = pool;
     return VA_OK;
 }
 
@@ -557,6 +775,8 @@ int db_create_impl(va_context* ctx, const void* rows, int on_device, int64_t n, 
     cudaError_t e = cudaMalloc(&db->rows, bytes);
     if (e == cudaSuccess) e = cudaMalloc((void**)&db->norms2, (size_t)n_pad * 4);
     if (e == cudaSuccess) e = cudaMalloc((void**)&db->zbias, (size_t)n_pad * 4);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&db->cert, VA_CERT_WORDS * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemsetAsync(db->cert, 0, VA_CERT_WORDS * sizeof(uint32_t), ctx->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         va_db_destroy(db);
@@ -568,7 +788,8 @@ int db_create_impl(va_context* ctx, const void* rows, int on_device, int64_t n, 
         va_db_destroy(db);
         return va_set_error(VA_ERR_CUDA, "database upload failed: %s", cudaGetErrorString(e));
     }
-    k_row_bias<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2, db->zbias);
+    k_row_bias<<<warps_grid(n_pad), 256, 0, ctx->stream>>>(db->rows, dtype, n, n_pad, dim, db->norms2, db->zbias,
+                                                           db->cert);
     int s = va_check_launch("k_row_bias");
     if (s == VA_OK && eager_operand) {
         // The bf16 operand serves the default precision: build it now so searches only read.
@@ -606,6 +827,7 @@ int va_db_destroy(va_database* db) {
     if (db->code_norms) cudaFree(db->code_norms);
     if (db->sq_mins) cudaFree(db->sq_mins);
     if (db->sq_scales) cudaFree(db->sq_scales);
+    if (db->cert) cudaFree(db->cert);
     if (db->rows) cudaFree(db->rows);
     delete db;
     return VA_OK;
@@ -642,39 +864,25 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     VA_CUDA_TRY(cudaEventRecord(ctx->ev_start, ctx->stream));
     ctx->k_recorded = false;
-    // Pools above 128 need fp32 rows: queries whose pool cannot be proven exact take the FP32 route.
-    int pool = choose_pool(k, rerank);
-    if (pool > 128 && db->dtype != VA_DTYPE_F32) pool = 0;
-    int prec = precision;
-    // AUTO: bf16 when the pool holds at least 3k candidates. Without a caller's factor, fp32 rows
-    // take a 3k pool (wider than 128 from k = 43 on) to stay on bf16; otherwise (bf16 rows, a thin
-    // caller-set pool) the 4x smaller tf32 error keeps the true top k inside the pool. No pool
-    // size -> exact FP32 route. Rows of at most 16 dimensions (fp32) take the FP32 route too: few
-    // dimensions give the reduced-precision keys no resolution between close neighbours (for
-    // d = 1 a bf16 key cannot order points 1/N apart), and the SIMT route is cheap there.
-    if (prec == VA_PREC_AUTO) {
-        if (pool && pool < 3 * k && rerank == 0 && db->dtype == VA_DTYPE_F32 && 3 * k <= VA_MAX_SELECT_K)
-            pool = 3 * k;
-        prec = !pool ? VA_PREC_FP32 : (pool >= 3 * k ? VA_PREC_BF16 : VA_PREC_TF32);
-        if (db->dim <= 16 && db->dtype == VA_DTYPE_F32) prec = VA_PREC_FP32;
-    }
-    if (prec == VA_PREC_FP32 && db->dtype != VA_DTYPE_F32) {
-        if (!pool) return va_set_error(VA_ERR_UNSUPPORTED, "k %d needs the FP32 route, which needs fp32 rows", k);
-        prec = VA_PREC_BF16;
-    }
+    ctx->stat_uncertified = 0;
+    ctx->stat_exact = 0;
+    int prec = 0, pool = 0;
+    VA_TRY(plan_route(db, k, precision, rerank, &prec, &pool));
     if (prec == VA_PREC_FP32) {
-        VA_TRY(search_fp32(ctx, db, queries, nq, k, metric, out_vals, out_ids));
+        ctx->stat_exact = nq;
+        VA_TRY(search_exact(ctx, db, queries, nq, k, metric, out_vals, out_ids));
     } else {
-        if (!pool)
-            return va_set_error(VA_ERR_UNSUPPORTED,
-                                "candidate pool %lld of k %d is not supported by the tensor-core route (at most %d, "
-                                "above 128 with fp32 rows); use precision FP32",
-                                (long long)(rerank ? (int64_t)rerank * k : (int64_t)k + std::max(k / 4, 22)), k,
-                                VA_MAX_SELECT_K);
         const int elem = prec == VA_PREC_TF32 ? 4 : 2;
         VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, pool, out_vals, out_ids));
     }
     VA_CUDA_TRY(cudaEventRecord(ctx->ev_stop, ctx->stream));
+    return VA_OK;
+}
+
+int va_last_search_stats(va_context* ctx, int64_t* uncertified, int64_t* exact) {
+    VA_REQUIRE(ctx && uncertified && exact, "ctx, uncertified and exact must not be NULL");
+    *uncertified = ctx->stat_uncertified;
+    *exact = ctx->stat_exact;
     return VA_OK;
 }
 
@@ -739,35 +947,53 @@ int noalloc_scratch(int device, void** out) {
     return VA_OK;
 }
 
-// Same steps as search_tc, with the scratch carved from a caller-provided region.
+// Same steps as search_tc (pass 1 with the certificate), with the scratch carved from a
+// caller-provided region; queries the pass cannot certify take the exact route inside the same
+// region (the pass's lists are dead by then).
+// Scratch bytes of search_tc_fixed's pass: fail count and list, query operand, lists, one bound
+// slot per query, pacing counters.
+int fixed_bytes(va_context* ctx, va_database* db, int64_t nq, int kp, int elem, TcPlan* plan, size_t* bytes) {
+    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, plan, (int64_t)db->dpad * elem));
+    const size_t head = 256 + round_up(4 * nq, 256);
+    const size_t q_bytes = (size_t)plan->nq_pad * db->dpad * elem;
+    const size_t part = (size_t)plan->splits * plan->nq_pad * kp;
+    *bytes = head + round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan->nq_pad * 4 +
+             (size_t)plan->sync_words * 4;
+    return VA_OK;
+}
+
 int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric, int elem,
                     int kp, uint8_t* scratch, size_t scratch_bytes, float* out_vals, uint32_t* out_ids) {
     TcPlan plan;
-    VA_TRY(va_tc_plan(ctx, nq, db->n, kp, &plan, (int64_t)db->dpad * elem));
+    size_t bytes = 0;
+    VA_TRY(fixed_bytes(ctx, db, nq, kp, elem, &plan, &bytes));
     const bool cosine = metric == VA_METRIC_COSINE;
     const void* x_op = elem == 2 ? (cosine ? (const void*)db->op_cos : (const void*)db->op)
                                  : (cosine ? (const void*)db->op_f32_cos : (const void*)db->op_f32);
-    if (!x_op)
+    const int kind = cert_kind(elem, cosine);
+    if (!x_op || !(db->cert_ready & (1u << kind)))
         return va_set_error(VA_ERR_UNSUPPORTED,
                             "the %s operand of this database is not built yet and building it would allocate; run "
                             "one va_knn_search with this metric and precision first",
                             elem == 2 ? (cosine ? "unit-norm bf16" : "bf16") : (cosine ? "unit-norm fp32" : "fp32"));
+    const size_t head = 256 + round_up(4 * nq, 256);  // fail count + fail list
     const size_t q_bytes = (size_t)plan.nq_pad * db->dpad * elem;
     const size_t part = (size_t)plan.splits * plan.nq_pad * kp;
-    const size_t bytes =
-        round_up((int64_t)q_bytes, 256) + part * 8 + (size_t)plan.nq_pad * 4 + (size_t)plan.sync_words * 4;
     if (bytes > scratch_bytes)
         return va_set_error(VA_ERR_INVALID_ARG,
-                            "numQueries %lld at dimension %d needs %zu bytes of scratch; the allocation-free search "
-                            "has %zu (split the batch)",
-                            (long long)nq, db->dim, bytes, scratch_bytes);
-    uint8_t* p = scratch;
+                            "numQueries %lld at dimension %d with a pool of %d needs %zu bytes of scratch; the "
+                            "allocation-free search has %zu (split the batch)",
+                            (long long)nq, db->dim, kp, bytes, scratch_bytes);
+    uint32_t* fail_cnt = (uint32_t*)scratch;
+    uint32_t* fail_list = (uint32_t*)(scratch + 256);
+    uint8_t* p = scratch + head;
     void* q_op = p;
     p += round_up((int64_t)q_bytes, 256);
     float* part_keys = (float*)p;
     uint32_t* part_ids = (uint32_t*)(part_keys + part);
     uint32_t* gthr = part_ids + part;
     uint32_t* sync_cnt = gthr + plan.nq_pad;
+    VA_CUDA_TRY(cudaMemsetAsync(fail_cnt, 0, 4, ctx->stream));
     if (elem == 2)
         k_operand<uint16_t><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (uint16_t*)q_op);
@@ -775,22 +1001,29 @@ int search_tc_fixed(va_context* ctx, va_database* db, const float* queries, int6
         k_operand<float><<<warps_grid(plan.nq_pad), 256, 0, ctx->stream>>>(
             queries, VA_DTYPE_F32, nq, plan.nq_pad, db->dim, db->dpad, cosine ? 1 : 0, (float*)q_op);
     VA_TRY(va_check_launch("k_operand(queries)"));
-    TcFilterArgs a = {};
-    a.q_op = q_op;
-    a.x_op = x_op;
-    a.elem_bytes = elem;
-    a.dpad = db->dpad;
-    a.n_rows = db->n;
-    a.row_bias = metric == VA_METRIC_L2SQ ? db->norms2 : db->zbias;
-    a.alpha = metric == VA_METRIC_L2SQ ? -2.f : -1.f;
-    a.part_keys = part_keys;
-    a.part_ids = part_ids;
-    a.gthr = gthr;          // va_tc_filter resets it before the launch
-    a.sync_cnt = sync_cnt;  // likewise
-    a.sync_words = plan.sync_words;
-    a.limit_ms = 2000u;
+    const TcFilterArgs a = filter_args(db, metric, elem, q_op, x_op, plan, part_keys, part_ids, gthr, sync_cnt);
     VA_TRY(va_tc_filter(ctx, a, plan));
-    return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids);
+    VA_TRY(merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, 0, 0,
+                        cert_args(db, elem, metric), fail_list, fail_cnt));
+    uint32_t nf = 0;
+    VA_TRY(read_count(ctx, fail_cnt, &nf));
+    ctx->stat_uncertified = nf;
+    ctx->stat_exact = nf;
+    if (!nf) return VA_OK;
+    // Exact route for the uncertified queries: gathered queries, their results, then the route's
+    // own scratch, all after the fail list.
+    uint8_t* r = scratch + head;
+    float* gq = (float*)r;
+    r += round_up((int64_t)nf * db->dim * 4, 256);
+    float* gv = (float*)r;
+    r += round_up((int64_t)nf * k * 4, 256);
+    uint32_t* gi = (uint32_t*)r;
+    r += round_up((int64_t)nf * k * 4, 256);
+    if (r >= scratch + scratch_bytes)
+        return va_set_error(VA_ERR_INVALID_ARG, "%u uncertified queries do not fit the allocation-free scratch", nf);
+    VA_TRY(gather_queries(ctx, queries, db->dim, fail_list, nf, gq));
+    VA_TRY(search_exact(ctx, db, gq, nf, k, metric, gv, gi, r, (size_t)(scratch + scratch_bytes - r)));
+    return scatter_results(ctx, gv, gi, fail_list, nf, k, out_vals, out_ids);
 }
 
 }  // namespace
@@ -811,12 +1044,37 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
     va_database* db = const_cast<va_database*>(cdb);
     VA_REQUIRE(db->ctx->device == ctx->device, "database lives on device %d, context on device %d", db->ctx->device,
                ctx->device);
-    const int kp = choose_kp(k, rerank);
-    VA_REQUIRE(kp > 0, "candidate pool of k %d exceeds the tensor-core filter's 128", k);
+    // The same route as va_knn_search (AUTO resolved identically); only its tensor-core form with
+    // pools of at most 128 candidates runs here.
+    int prec = 0, pool = 0;
+    VA_TRY(plan_route(db, k, precision, rerank, &prec, &pool));
+    if (prec == VA_PREC_FP32)
+        return va_set_error(VA_ERR_UNSUPPORTED,
+                            "k %d at dimension %d takes the exact FP32 route under AUTO, which allocates; pass "
+                            "precision BF16 or TF32, or use va_knn_search",
+                            k, db->dim);
+    if (k > 128)
+        return va_set_error(VA_ERR_UNSUPPORTED,
+                            "k %d exceeds the allocation-free search's lists of at most 128 entries; use "
+                            "va_knn_search",
+                            k);
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
+    const int elem = prec == VA_PREC_TF32 ? 4 : 2;
+    // Lists of the route's pool (at most 128 entries), halved while the batch does not fit the
+    // array but never below k: the results stay exact, since the certificate sends every query
+    // a thinner pool cannot prove to the exact route.
+    int kp = choose_kp(std::min(pool, 128), 1);
+    for (;;) {
+        TcPlan plan;
+        size_t bytes = 0;
+        VA_TRY(fixed_bytes(ctx, db, nq, kp, elem, &plan, &bytes));
+        if (bytes <= VA_NOALLOC_SCRATCH_BYTES || kp == 32 || kp / 2 < k) break;
+        kp /= 2;
+    }
+    ctx->stat_uncertified = 0;
+    ctx->stat_exact = 0;
     void* scratch = nullptr;
     VA_TRY(noalloc_scratch(ctx->device, &scratch));
-    const int elem = precision == VA_PREC_TF32 ? 4 : 2;
     return search_tc_fixed(ctx, db, queries, nq, k, metric, elem, kp, (uint8_t*)scratch, VA_NOALLOC_SCRATCH_BYTES,
                            out_vals, out_ids);
 }
@@ -833,9 +1091,11 @@ int va_db_derive_rows(va_context* ctx, va_database* db, int64_t r0, int64_t coun
     const int64_t pad_end = r0 + count >= db->n ? round_up(db->n, 256) : r0 + count;
     if (db->norms2) {
         k_row_bias<<<warps_grid(pad_end - r0), 256, 0, ctx->stream>>>(src, db->dtype, count, pad_end - r0, db->dim,
-                                                                      db->norms2 + r0, db->zbias + r0);
+                                                                      db->norms2 + r0, db->zbias + r0, db->cert);
         VA_TRY(va_check_launch("k_row_bias(append)"));
     }
+    for (int kind = 0; kind < 4; ++kind)
+        if (db->cert_ready & (1u << kind)) VA_TRY(operand_err(ctx, db, kind, r0, count));
     const int64_t dp = db->dpad;
     if (db->op && !db->op_alias)
         k_operand<uint16_t><<<warps_grid(count), 256, 0, ctx->stream>>>(src, db->dtype, count, count, db->dim, db->dpad,
@@ -853,10 +1113,13 @@ int va_db_derive_rows(va_context* ctx, va_database* db, int64_t r0, int64_t coun
 }
 
 // Internal entry of the merge + exact rerank step for other translation units (the int8 path).
+// Internal entry of the merge + exact rerank step for other translation units (the int8 path,
+// whose integer keys are exact: no certificate; fail_list set = prove a pool wider than the lists).
 int va_merge_rerank_internal(va_context* ctx, va_database* db, const float* queries, int64_t nq, int k, int metric,
                              const TcPlan& plan, const float* part_keys, const uint32_t* part_ids,
                              const uint32_t* gthr, float* out_vals, uint32_t* out_ids, int pool_n,
                              uint32_t* fail_list, uint32_t* fail_cnt) {
+    CertArgs off = {};
     return merge_rerank(ctx, db, queries, nq, k, metric, plan, part_keys, part_ids, gthr, out_vals, out_ids, pool_n,
-                        fail_list, fail_cnt);
+                        fail_list ? 1 : 0, off, fail_list, fail_cnt);
 }

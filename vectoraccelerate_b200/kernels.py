@@ -525,6 +525,12 @@ class HammingDistanceKernel(_Kernel):
 
 
 class _DbHandle:
+    def rows_ptr(self) -> int:
+        """Device pointer of the stored rows: fp32 rows of an int8 database, packed codes of a binary one."""
+        p = ctypes.c_void_p()
+        _ffi.call("va_db_rows", self.handle, ctypes.byref(p))
+        return p.value
+
     def close(self):
         if getattr(self, "handle", None):
             _ffi.call("va_db_destroy", self.handle)
