@@ -55,6 +55,7 @@ def parse_args():
     p.add_argument("--nq", type=int, default=10_000)
     p.add_argument("--k", type=int, default=10)
     p.add_argument("--precision", choices=["bf16", "tf32", "fp32"], default="bf16")
+    p.add_argument("--rerank", type=int, default=0, help="headline: candidate-pool factor (0 = automatic)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the oracle parity check of sampled queries")
     p.add_argument("--parity-queries", type=int, default=PARITY_QUERIES)
@@ -463,7 +464,7 @@ def run_ours(a):
     qptr = [dq.data_ptr()]
 
     def local_search(nq, kk):
-        _ffi.call("va_knn_search", ctx.handle, db.handle, qptr[0], nq, kk, va.METRIC_L2SQ, prec, 0,
+        _ffi.call("va_knn_search", ctx.handle, db.handle, qptr[0], nq, kk, va.METRIC_L2SQ, prec, a.rerank,
                   lv.data_ptr(), li.data_ptr())
         return lv, li
 
@@ -477,7 +478,7 @@ def run_ours(a):
     def step_e2e():
         if world == 1:
             _ffi.call("va_knn_search_host", ctx.handle, db.handle, ctypes.c_void_p(hq.data_ptr()), a.nq, k,
-                      va.METRIC_L2SQ, prec, 0, ctypes.c_void_p(hv.data_ptr()), ctypes.c_void_p(hi.data_ptr()))
+                      va.METRIC_L2SQ, prec, a.rerank, ctypes.c_void_p(hv.data_ptr()), ctypes.c_void_p(hi.data_ptr()))
         else:
             dq.copy_(hq, non_blocking=True)
             step_device(dq.data_ptr())

@@ -45,7 +45,7 @@ def _search(ctx, x, q, k, metric=0, precision=0, rerank=0, dtype=0):
 @pytest.mark.parametrize("metric", [0, 1, 2])
 @pytest.mark.parametrize("precision", [2, 3])
 def test_runs_beyond_every_pool_take_the_exact_route(ctx, oracle, metric, precision):
-    # 300 near-duplicates: neither the first pool (32) nor the second (128) separates them.
+    # 300 near-duplicates: neither the first pool (32) nor the second (64) separates them.
     x, q = _near_duplicate_db(20_000, 128, 300, seed=11 + metric, normalize=metric == 1)
     vals, ids, (unc, exact) = _search(ctx, x, q, 10, metric=metric, precision=precision)
     assert unc >= 4 and exact >= 4, (unc, exact)
@@ -53,8 +53,8 @@ def test_runs_beyond_every_pool_take_the_exact_route(ctx, oracle, metric, precis
 
 
 def test_runs_inside_the_second_pool_are_certified_there(ctx, oracle):
-    # 60 near-duplicates: the first pool (32) cannot separate them, the second (128) holds them all.
-    x, q = _near_duplicate_db(20_000, 128, 60, seed=5)
+    # 50 near-duplicates: the first pool (32) cannot separate them, the second (64) holds them all.
+    x, q = _near_duplicate_db(20_000, 128, 50, seed=5)
     vals, ids, (unc, exact) = _search(ctx, x, q, 10, precision=3)
     assert unc >= 4 and exact == 0, (unc, exact)
     _check(oracle, q, x, 10, 0, vals, ids)

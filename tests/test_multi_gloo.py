@@ -85,3 +85,50 @@ def test_shard_bounds_cover_rows():
             for (a, na), (b, _) in zip(spans, spans[1:]):
                 assert a + na == b
             assert spans[-1][0] + spans[-1][1] == n
+
+
+# ------------------------------------------------------------------------------------------------ failures
+def _join_or_fail(rank, world, port, mode, out):
+    """mode 'never_joins': rank 1 exits without joining; 'raises': rank 1 joins, then raises before
+    the gather. Rank 0 reports how its next step ended and after how long."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if mode == "never_joins" and rank == 1:
+        return
+    t0 = time.time()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+        if mode == "raises" and rank == 1:
+            dist.destroy_process_group()
+            raise SystemExit(3)
+        from vectoraccelerate_b200.sharded import ShardedSearch
+
+        def local(nq, k):
+            return torch.zeros((nq, k)), torch.zeros((nq, k), dtype=torch.int32)
+
+        ShardedSearch(world, local, lambda gv, gi: (gv[0], gi[0])).search(4, 2)
+        out.put(("completed", time.time() - t0))
+    except Exception as e:  # the bounded error this test expects
+        out.put((type(e).__name__, time.time() - t0))
+
+
+@pytest.mark.parametrize("mode", ["never_joins", "raises"])
+def test_missing_rank_gives_a_bounded_error(mode):
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_join_or_fail, args=(r, 2, port, mode, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    what, seconds = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert what != "completed", "rank 0 finished a collective without its peer"
+    assert seconds < 60, f"rank 0 waited {seconds:.1f} s"

@@ -471,10 +471,14 @@ int choose_pool(int k, int rerank) {
     return want <= VA_MAX_SELECT_K ? (int)want : 0;
 }
 
-// Pool of the second tensor-core pass over the queries the first pass could not certify: at least
-// four times wider (and at least 128); 0 when no wider pool is supported (exact route next).
+// Pool of the second tensor-core pass over the queries the first pass could not certify: the next
+// list size (32 -> 64 -> 128 entries: each doubling adds about ln 2 extreme-value spacings to the
+// certificate's gap, and the pass over a few query tiles costs little), then four times wider
+// (pools proven from 64/128-entry lists); 0 when no wider pool is supported (exact route next).
 int wider_pool(int pool) {
-    const int p = std::min(std::max(4 * pool, 128), VA_MAX_SELECT_K);
+    if (pool < 64) return 64;
+    if (pool < 128) return 128;
+    const int p = std::min(4 * pool, VA_MAX_SELECT_K);
     return p > pool ? p : 0;
 }
 

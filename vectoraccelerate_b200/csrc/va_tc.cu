@@ -95,6 +95,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Teardown after an abort: wait (bounded by limit_ns, ignoring the abort flag) for a phase that
+// work already in flight will complete: a TMA load's bytes landing, or a tcgen05.commit.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return;
+    const uint64_t t0 = va::globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (va::globaltimer_ns() - t0 > limit_ns) return;
+}
+
+// Bound of each teardown wait: in-flight copies and MMAs finish within microseconds.
+constexpr uint64_t kDrainLimitNs = 1000000000ull;
+
+// The producer's teardown after an abort: every TMA load it issued into the stage ring (the last
+// min(stages, issued) iterations) has landed before the CTA may exit.
+__device__ __forceinline__ void drain_loads(uint64_t* full, int stages, uint32_t issued) {
+    const uint32_t first = issued > (uint32_t)stages ? issued - (uint32_t)stages : 0u;
+    for (uint32_t i = first; i < issued; ++i) mbar_drain(&full[i % stages], (i / stages) & 1u, kDrainLimitNs);
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
@@ -433,6 +452,9 @@ struct Work {
     const int* row_pair;
     int pair_div;
     int item_base;  // list mode: item i is query tile item_base + i
+    // Test hook (VA_TC_TEST_STALL_TILES): the MMA issuer stops after this many tiles, so the
+    // epilogue's bounded wait for the next accumulator expires; -1 in every real launch.
+    int stall_tiles;
 };
 
 __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
@@ -507,7 +529,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* empty = bars + stages;
     uint64_t* tfull = bars + 2 * stages;
     uint64_t* tempty = tfull + 2;
-    uint32_t* s_tmem = (uint32_t*)(tempty + 2);
+    uint64_t* dbar = tempty + 2;  // teardown: the MMA issuer's final commit
+    uint32_t* s_tmem = (uint32_t*)(dbar + 1);
     volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -522,6 +545,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 4);
         }
+        mbar_init(dbar, 1);
         *s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
@@ -579,7 +603,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (w.sync_cnt)
                     for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
             }
-        producer_done:;
+        producer_done:
+            // After an abort, loads still in flight write this CTA's shared memory: wait for them.
+            if (*s_abort) drain_loads(full, stages, it);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
@@ -591,6 +617,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t re;
                 item_rows(w, item, qt, t0, t1, rb, re);
                 for (int t = t0; t < t1; ++t, ++tile) {
+                    if ((int)tile == w.stall_tiles) goto mma_done;
                     const uint32_t buf = tile & 1u;
                     const uint32_t tph = (tile >> 1) & 1u;
                     if (!mbar_wait(&tempty[buf], tph ^ 1u, s_abort, err, limit_ns)) goto mma_done;
@@ -613,7 +640,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     mma_commit(&tfull[buf]);
                 }
             }
-        mma_done:;
+        mma_done:
+            // After an abort (or a stall), MMAs already issued may still write TMEM: one more
+            // commit tracks all of them; wait for it before TMEM is freed.
+            if (*s_abort || w.stall_tiles >= 0) {
+                mma_commit(dbar);
+                mbar_drain(dbar, 0u, kDrainLimitNs);
+            }
         }
     } else {
         // ---------------------------------------------------------------- epilogue (warps 2..5)
@@ -792,6 +825,19 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
                  : "memory");
 }
+// An abort in one CTA of a pair stops both: its flag is also set in the peer CTA.
+__device__ __forceinline__ void abort_peer(volatile int* s_abort, uint32_t rank) {
+    *s_abort = 1;
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_rank(smem_u32((const void*)s_abort), rank ^ 1u)), "r"(1)
+                 : "memory");
+}
+// Teardown of a pair after an abort: a CTA's TMA loads signal the leader's barriers, so the peer
+// cannot wait for its own loads; both CTAs let in-flight copies land (a fixed settle time, far
+// above a copy's latency) before the cluster barrier that precedes TMEM release and exit.
+__device__ __forceinline__ void settle_ns(uint64_t ns) {
+    const uint64_t t0 = va::globaltimer_ns();
+    while (va::globaltimer_ns() - t0 < ns) __nanosleep(1000);
+}
 
 template <int ELEM>
 struct PairKind;
@@ -850,7 +896,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* empty = bars + stages;
     uint64_t* tfull = bars + 2 * stages;
     uint64_t* tempty = tfull + 2;
-    uint32_t* s_tmem = (uint32_t*)(tempty + 2);
+    uint64_t* dbar = tempty + 2;  // teardown: the leader's final pair commit
+    uint32_t* s_tmem = (uint32_t*)(dbar + 1);
     volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -868,6 +915,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 8);
         }
+        mbar_init(dbar, 1);
         *s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
@@ -910,7 +958,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int kb = 0; kb < w.k_blocks; ++kb, ++it) {
                         const int s = it % stages;
                         const uint32_t ph = (it / stages) & 1u;
-                        if (!mbar_wait(&empty[s], ph ^ 1u, s_abort, err, limit_ns)) goto producer_done;
+                        if (!mbar_wait(&empty[s], ph ^ 1u, s_abort, err, limit_ns)) {
+                            abort_peer(s_abort, rank);
+                            goto producer_done;
+                        }
                         const uint32_t full_leader = map_rank(smem_u32(&full[s]), 0);
                         if (leader) mbar_expect_tx(&full[s], 2 * PSTAGE_BYTES);
                         const int kc = kb * (BKB / ELEM);
@@ -922,7 +973,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 for (int c = next_slot; c < w.cpr; ++c) atomicAdd(w.sync_cnt + round * w.cpr + c, 1u);
             }
-        producer_done:;
+        producer_done:
+            if (*s_abort) {
+                // The leader's full barriers count both CTAs' bytes of every stage it armed.
+                if (leader) drain_loads(full, stages, it);
+                settle_ns(1000000ull);
+            }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer (leader only)
@@ -934,13 +990,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int t = t0; t < t1; ++t, ++tile) {
                     const uint32_t buf = tile & 1u;
                     const uint32_t tph = (tile >> 1) & 1u;
-                    if (!mbar_wait(&tempty[buf], tph ^ 1u, s_abort, err, limit_ns)) goto mma_done;
+                    if (!mbar_wait(&tempty[buf], tph ^ 1u, s_abort, err, limit_ns)) {
+                        abort_peer(s_abort, rank);
+                        goto mma_done;
+                    }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + buf * BN;
                     for (int kb = 0; kb < w.k_blocks; ++kb, ++it) {
                         const int s = it % stages;
                         const uint32_t ph = (it / stages) & 1u;
-                        if (!mbar_wait(&full[s], ph, s_abort, err, limit_ns)) goto mma_done;
+                        if (!mbar_wait(&full[s], ph, s_abort, err, limit_ns)) {
+                            abort_peer(s_abort, rank);
+                            goto mma_done;
+                        }
                         tc_fence_after();
                         const uint32_t a0 = smem_u32(sA + (size_t)s * PA_BYTES);
                         const uint32_t b0 = smem_u32(sB + (size_t)s * PB_BYTES);
@@ -957,7 +1019,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     mma_commit_pair(map_rank(f, 1));
                 }
             }
-        mma_done:;
+        mma_done:
+            if (*s_abort) {
+                // pair MMAs already issued write both CTAs' TMEM: wait for all of them
+                mma_commit_pair(map_rank(smem_u32(dbar), 0));
+                mbar_drain(dbar, 0u, kDrainLimitNs);
+            }
         }
     } else {
         // ---------------------------------------------------------------- epilogue (both CTAs)
@@ -998,7 +1065,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint32_t buf = tile & 1u;
                 const uint32_t tph = (tile >> 1) & 1u;
                 int ok = 1;
-                if (lane == 0) ok = mbar_wait(&tfull[buf], tph, s_abort, err, limit_ns) ? 1 : 0;
+                if (lane == 0) {
+                    ok = mbar_wait(&tfull[buf], tph, s_abort, err, limit_ns) ? 1 : 0;
+                    if (!ok) abort_peer(s_abort, rank);
+                }
                 ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
                 if (!ok) goto epi_done;
                 tc_fence_after();
@@ -1051,6 +1121,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
     }
+}
+
+// Test hooks of the bounded-wait path, read at every launch: VA_TC_WAIT_LIMIT_MS replaces the
+// device waits' limit; VA_TC_TEST_STALL_TILES makes the single-CTA kernel's MMA issuer stop after
+// that many tiles (the pair kernel ignores it), so a bounded wait expires and the launch reports
+// VA_ERR_TIMEOUT through va_synchronize. Unset in normal use.
+uint64_t wait_limit_ns(unsigned limit_ms) {
+    const char* e = getenv("VA_TC_WAIT_LIMIT_MS");
+    const long v = e ? atol(e) : 0;
+    return (uint64_t)(v > 0 ? (unsigned long)v : limit_ms) * 1000000ull;
+}
+
+int test_stall_tiles() {
+    const char* e = getenv("VA_TC_TEST_STALL_TILES");
+    return e && e[0] ? std::max(0, atoi(e)) : -1;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -1111,14 +1196,14 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
     cfg.attrs = attr;
     cfg.numAttrs = pair ? 2 : 1;
     VA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mq, mx, w, a.row_bias, a.alpha, a.row_qn, a.part_keys, a.part_ids,
-                                   a.gthr, ctx->d_error, (uint64_t)a.limit_ms * 1000000ull, stages));
+                                   a.gthr, ctx->d_error, wait_limit_ns(a.limit_ms), stages));
     return va_check_launch(pair ? "k_tc_filter_pair" : "k_tc_filter");
 }
 
 size_t smem_bytes(int kp, int stages, bool pair) {
     const int stride = kp <= 64 ? kp + 1 : kp;  // list_stride<KP>()
     return 1024 + (size_t)stages * (pair ? PSTAGE_BYTES : STAGE_BYTES) + (size_t)stride * BM * 8 +
-           (2 * stages + 4) * 8 + 16;
+           (2 * stages + 5) * 8 + 16;
 }
 
 }  // namespace
@@ -1255,6 +1340,7 @@ int va_tc_filter(va_context* ctx, const TcFilterArgs& a, const TcPlan& p) {
     w.pair_div = 1;
     w.item_base = 0;
     w.lv = a.levels.n > 0 ? a.levels : one_level(p.kp);
+    w.stall_tiles = test_stall_tiles();
     for (int l = 0; l < w.lv.n; ++l)
         if (w.lv.rank[l] < 1 || w.lv.rank[l] > p.kp || w.lv.slots[l] < 1)
             return va_set_error(VA_ERR_INVALID_ARG, "bound level %d: rank %d / slots %d invalid for lists of %d", l,
@@ -1315,6 +1401,7 @@ int va_tc_filter_lists(va_context* ctx, const TcFilterArgs& a, int n_qtiles, int
     w.row_pair = row_pair;
     w.pair_div = pair_div;
     w.item_base = tile0;
+    w.stall_tiles = -1;
     const int stages = va_tc_stages(kp, false);
     if (stages < 2) return va_set_error(VA_ERR_UNSUPPORTED, "list length %d too large for shared memory", kp);
     const size_t smem = smem_bytes(kp, stages, false);
