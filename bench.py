@@ -417,6 +417,28 @@ def profiled_traffic():
         return None
 
 
+def make_context(va, dist, rank, world, local, stream):
+    """The library context of this rank: a plain one-device context at N = 1, else one rank of an
+    NCCL group (va_context_create_rank; rank 0's unique id reaches the others through the process
+    group's broadcast)."""
+    cfg = va.Metal4Configuration(device=local, stream=stream.cuda_stream)
+    if world == 1:
+        return va.GPUContext(cfg)
+    nid = [va.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(nid, src=0)
+    return va.GPUContext.rank(world, rank, nid[0], cfg)
+
+
+def launches_per_step(ctx, world: int, precision: str):
+    """Kernels of this library in one step (from the last search's certificate counts): query
+    operand, filter, merge + rerank; a second pass (gather, operand, filter, merge, scatter) when
+    some query was not certified; pack, unpack and shard merge on N > 1 GPUs. None on the FP32 route."""
+    if precision == "fp32":
+        return None
+    unc, _ = ctx.last_search_stats()
+    return 3 + (5 if unc else 0) + (3 if world > 1 else 0)
+
+
 # ------------------------------------------------------------------------------------------ ours
 def run_ours(a):
     import torch
@@ -434,16 +456,17 @@ def run_ours(a):
     # stream would make the library create its own, unordered with the timing events).
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
-    ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
+    ctx = make_context(va, dist, rank, world, local, stream)
     prec = {"bf16": va.PREC_BF16, "tf32": va.PREC_TF32, "fp32": va.PREC_FP32}[a.precision]
 
-    from vectoraccelerate_b200.sharded import ShardedSearch, device_merge, shard_bounds
-
-    # ---- database shard, generated on the device, built into a resident va_database
-    row0, n_local = shard_bounds(a.n, world, rank)
+    # ---- database shard, generated on the device, built into a resident (sharded) va_database
+    row0, n_local = ctx.shard_range(a.n) if world > 1 else (0, a.n)
     gen = torch.empty((n_local, a.dim), dtype=torch.float32, device="cuda")
     _ffi.call("va_gen_gaussian", ctx.handle, gen.data_ptr(), n_local, a.dim, 0, row0)
-    db = va.Database(ctx, None, device_ptr=gen.data_ptr(), n=n_local, dim=a.dim, id_base=row0)
+    if world > 1:
+        db = va.ShardedDatabase(ctx, device_ptr=gen.data_ptr(), n=a.n, dim=a.dim)
+    else:
+        db = va.Database(ctx, None, device_ptr=gen.data_ptr(), n=n_local, dim=a.dim)
     ctx.synchronize()
     del gen
     torch.cuda.empty_cache()
@@ -458,32 +481,17 @@ def run_ours(a):
     li = torch.empty((a.nq, k), dtype=torch.int32, device="cuda")
     hv = torch.empty((a.nq, k), dtype=torch.float32).pin_memory()
     hi = torch.empty((a.nq, k), dtype=torch.int32).pin_memory()
-    launches_per_step = 3 + (1 if world > 1 else 0)  # query operand, filter, merge+rerank (+ shard merge)
-    if prec == va.PREC_FP32:
-        launches_per_step = None
-    qptr = [dq.data_ptr()]
-
-    def local_search(nq, kk):
-        _ffi.call("va_knn_search", ctx.handle, db.handle, qptr[0], nq, kk, va.METRIC_L2SQ, prec, a.rerank,
-                  lv.data_ptr(), li.data_ptr())
-        return lv, li
-
-    sharded = ShardedSearch(world, local_search, device_merge(ctx, world, a.nq, k))
     final = [lv, li]
 
+    # One step = va_knn_search over the whole database: on N > 1 GPUs each rank's library call
+    # searches its shard, all-gathers packed (value, id) records over NCCL and merges on the device.
     def step_device(queries_ptr):
-        qptr[0] = queries_ptr
-        final[0], final[1] = sharded.search(a.nq, k)
+        _ffi.call("va_knn_search", ctx.handle, db.handle, queries_ptr, a.nq, k, va.METRIC_L2SQ, prec, a.rerank,
+                  lv.data_ptr(), li.data_ptr())
 
     def step_e2e():
-        if world == 1:
-            _ffi.call("va_knn_search_host", ctx.handle, db.handle, ctypes.c_void_p(hq.data_ptr()), a.nq, k,
-                      va.METRIC_L2SQ, prec, a.rerank, ctypes.c_void_p(hv.data_ptr()), ctypes.c_void_p(hi.data_ptr()))
-        else:
-            dq.copy_(hq, non_blocking=True)
-            step_device(dq.data_ptr())
-            hv.copy_(final[0], non_blocking=True)
-            hi.copy_(final[1], non_blocking=True)
+        _ffi.call("va_knn_search_host", ctx.handle, db.handle, ctypes.c_void_p(hq.data_ptr()), a.nq, k,
+                  va.METRIC_L2SQ, prec, a.rerank, ctypes.c_void_p(hv.data_ptr()), ctypes.c_void_p(hi.data_ptr()))
 
     def barrier_sync():
         torch.cuda.synchronize()
@@ -535,16 +543,17 @@ def run_ours(a):
     e1.record(stream)
     barrier_sync()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-    if world == 1:
-        # va_knn_search_host runs on the context stream and waits; bracket with wall time too
-        t0 = time.perf_counter()
-        for _ in range(a.steps):
-            step_e2e()
-        e2e_ms = max(e2e_ms, (time.perf_counter() - t0) * 1e3 / a.steps)
+    # va_knn_search_host runs on the context stream and waits; bracket with wall time too
+    barrier_sync()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step_e2e()
+    e2e_ms = max(e2e_ms, max_over_ranks((time.perf_counter() - t0) * 1e3 / a.steps))
 
     # ---- certificate counts of one step's local search, and oracle parity of sampled queries
     step_device(dq.data_ptr())
     torch.cuda.synchronize()
+    lps = launches_per_step(ctx, world, a.precision)
     unc, exa = ctypes.c_int64(), ctypes.c_int64()
     _ffi.call("va_last_search_stats", ctx.handle, ctypes.byref(unc), ctypes.byref(exa))
     unc_all = all_gather_host(np.array([unc.value, exa.value], np.int64), world)
@@ -558,6 +567,8 @@ def run_ours(a):
         exactness["parity"] = oracle_parity("float", ctx, db, hq.numpy(), parity_sample(a.nq, a.parity_queries),
                                             vals_h, ids_h, k, 0, row0, n_local, a.n, a.dim, world)
 
+    db.close()
+    ctx.close()
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -591,7 +602,7 @@ def run_ours(a):
         "exactness": exactness,
         "e2e": {"value": a.nq / (e2e_ms * 1e-3), "unit": "queries/s",
                 "h2d_bytes_per_step": world * a.nq * a.dim * 4, "d2h_bytes_per_step": world * a.nq * k * 8},
-        "gpu_launches": launches_per_step * a.steps if launches_per_step else None,
+        "gpu_launches": (lps * a.steps) if lps else None,
         "roofline": roof,
         "clocks": clk,
     }
@@ -616,14 +627,14 @@ def auto_precision(k: int, rerank: int, f32_rows: bool = True) -> str:
 
 
 def run_config(a):
-    """One of the other BASELINE configurations on this rank's row shard (N/world rows, global
-    ids = shard base + row), all-gather + device merge for world > 1, as the headline."""
+    """One of the other BASELINE configurations; for N > 1 the database is sharded by the library
+    (N/world rows per rank, global ids = shard base + row) and each search all-gathers and merges
+    inside the library call, as the headline."""
     import torch
     import torch.distributed as dist
 
     import vectoraccelerate_b200 as va
     from vectoraccelerate_b200 import _ffi
-    from vectoraccelerate_b200.sharded import ShardedSearch, device_merge, shard_bounds
 
     c = CONFIGS[a.config]
     kind = c["kind"]
@@ -634,10 +645,10 @@ def run_config(a):
                                 device_id=torch.device("cuda", local))
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
-    ctx = va.GPUContext(va.Metal4Configuration(device=local, stream=stream.cuda_stream))
+    ctx = make_context(va, dist, rank, world, local, stream)
     n_total = a.n
     note = None
-    row0, n_local = shard_bounds(n_total, world, rank)
+    row0, n_local = ctx.shard_range(n_total) if world > 1 else (0, n_total)
     dim, nq, k = a.dim, a.nq, a.k
     chunk = max(1, (4 << 30) // (4 * dim))  # fp32 generation chunks of <= 4 GiB
 
@@ -649,7 +660,7 @@ def run_config(a):
             _ffi.call("va_gen_gaussian", ctx.handle, dst_ptr, rows, dim, seed, r0)
 
     db_seed, q_seed, q_row0 = (2, 3, 0) if kind == "binary" else (0, 0, QUERY_ROW0)
-    # ---- database shard
+    # ---- database shard (N > 1: this rank's rows of a database sharded by the library)
     if kind == "float" and c["rows"] == "bf16":
         rows = torch.empty((n_local, dim), dtype=torch.int16, device="cuda")
         tmp = torch.empty((min(chunk, n_local), dim), dtype=torch.float32, device="cuda")
@@ -660,26 +671,23 @@ def run_config(a):
         ctx.synchronize()
         del tmp
         torch.cuda.empty_cache()
-        db = va.Database(ctx, None, dtype=va.DTYPE_BF16, device_ptr=rows.data_ptr(), n=n_local, dim=dim,
-                         id_base=row0)
+        if world > 1:
+            db = va.ShardedDatabase(ctx, device_ptr=rows.data_ptr(), n=n_total, dim=dim, dtype=va.DTYPE_BF16)
+        else:
+            db = va.Database(ctx, None, dtype=va.DTYPE_BF16, device_ptr=rows.data_ptr(), n=n_local, dim=dim)
     elif kind in ("float", "int8"):
         rows = torch.empty((n_local, dim), dtype=torch.float32, device="cuda")
         for r in range(0, n_local, chunk):
             gen_f32(rows[r:].data_ptr(), min(chunk, n_local - r), db_seed, row0 + r)
         ctx.synchronize()
-        if kind == "float":
-            db = va.Database(ctx, None, device_ptr=rows.data_ptr(), n=n_local, dim=dim, id_base=row0)
+        if world > 1:
+            # int8: the library codes every shard with the per-dimension range of the WHOLE
+            # database (min / max all-reduced over the group)
+            db = va.ShardedDatabase(ctx, device_ptr=rows.data_ptr(), n=n_total, dim=dim, kind=kind)
+        elif kind == "float":
+            db = va.Database(ctx, None, device_ptr=rows.data_ptr(), n=n_local, dim=dim)
         else:
-            # per-dimension range over the WHOLE database: local min / max, then MIN / MAX all-reduce
-            mn = torch.empty(dim, dtype=torch.float32, device="cuda")
-            mx = torch.empty(dim, dtype=torch.float32, device="cuda")
-            _ffi.call("va_sq_perdim_minmax", ctx.handle, rows.data_ptr(), n_local, dim, mn.data_ptr(), mx.data_ptr())
-            torch.cuda.synchronize()
-            if world > 1:
-                dist.all_reduce(mn, op=dist.ReduceOp.MIN)
-                dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            db = va.Int8Database(ctx, None, id_base=row0, mins=mn.cpu().numpy(), maxs=mx.cpu().numpy(),
-                                 device_ptr=rows.data_ptr(), n=n_local, dim=dim)
+            db = va.Int8Database(ctx, None, device_ptr=rows.data_ptr(), n=n_local, dim=dim)
     else:
         words = dim // 32
         rows = torch.empty((n_local, words), dtype=torch.int32, device="cuda")
@@ -690,7 +698,10 @@ def run_config(a):
             _ffi.call("va_binary_quantize", ctx.handle, tmp.data_ptr(), m, dim, 0.0, rows[r:r + m].data_ptr())
         ctx.synchronize()
         del tmp
-        db = va.BinaryDatabase.from_device(ctx, rows.data_ptr(), n_local, dim, id_base=row0)
+        if world > 1:
+            db = va.ShardedDatabase(ctx, device_ptr=rows.data_ptr(), n=n_total, dim=dim, kind="binary")
+        else:
+            db = va.BinaryDatabase.from_device(ctx, rows.data_ptr(), n_local, dim)
     ctx.synchronize()
     del rows
     torch.cuda.empty_cache()
@@ -712,33 +723,26 @@ def run_config(a):
     hv = torch.empty((nq, k), dtype=torch.float32).pin_memory()
     hi = torch.empty((nq, k), dtype=torch.int32).pin_memory()
     metric = {"COSINE": va.METRIC_COSINE, "IP": va.METRIC_IP}.get(c.get("metric"), va.METRIC_L2SQ)
-    mode = 1 if metric == va.METRIC_IP and kind == "float" else 0
-
-    def local_search(nq_, kk):
-        if kind == "float":
-            _ffi.call("va_knn_search", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, metric, va.PREC_AUTO,
-                      c["rerank"], lv.data_ptr(), li.data_ptr())
-        elif kind == "int8":
-            _ffi.call("va_int8_knn_search", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, c["candidates"],
-                      lv.data_ptr(), li.data_ptr())
-        else:
-            # uint32 distances are written as their bit patterns into the float list; those order
-            # like the integers, so the float merge applies unchanged
-            _ffi.call("va_hamming_knn_db", ctx.handle, db.handle, dq.data_ptr(), nq_, kk, lv.data_ptr(),
-                      li.data_ptr())
-        return lv, li
-
-    sharded = ShardedSearch(world, local_search, device_merge(ctx, world, nq, k, mode=mode))
     final = [lv, li]
 
+    # One step = one library call over the whole database (sharded over the ranks for N > 1).
+    def search(qptr, ov, oi):
+        if kind == "float":
+            _ffi.call("va_knn_search", ctx.handle, db.handle, qptr, nq, k, metric, va.PREC_AUTO, c["rerank"], ov, oi)
+        elif kind == "int8":
+            _ffi.call("va_int8_knn_search", ctx.handle, db.handle, qptr, nq, k, c["candidates"], ov, oi)
+        else:
+            # uint32 distances land in the float array as their bit patterns
+            _ffi.call("va_hamming_knn_db", ctx.handle, db.handle, qptr, nq, k, ov, oi)
+
     def step():
-        final[0], final[1] = sharded.search(nq, k)
+        search(dq.data_ptr(), lv.data_ptr(), li.data_ptr())
 
     def step_e2e():
         dq.copy_(hq, non_blocking=True)
         step()
-        hv.copy_(final[0], non_blocking=True)
-        hi.copy_(final[1], non_blocking=True)
+        hv.copy_(lv, non_blocking=True)
+        hi.copy_(li, non_blocking=True)
 
     def barrier_sync():
         torch.cuda.synchronize()
@@ -808,6 +812,8 @@ def run_config(a):
                                             else hq.numpy(), parity_sample(nq, a.parity_queries), vals_h, ids_h,
                                             k, metric, row0, n_local, n_total, dim, world,
                                             candidates=c.get("candidates", 0), sq=sq)
+    db.close()
+    ctx.close()
     if rank != 0:
         if world > 1:
             dist.barrier()

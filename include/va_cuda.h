@@ -247,6 +247,57 @@ int va_knn_search_noalloc(va_context* ctx, const va_database* db, const float* q
                           int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids);
 
 /* ------------------------------------------------------------------------------------------ */
+/* Multi-GPU: row-sharded search over a group of devices (no reference counterpart: the        */
+/* reference's Metal4Context, Core/Metal4Context.swift:175,183, owns one device).              */
+/* ------------------------------------------------------------------------------------------ */
+/* A group joins several devices with an NCCL communicator (loaded at run time: libnccl.so.2, or
+ * the path in VA_NCCL_LIBRARY; VA_ERR_NCCL when absent). Its front context is an ordinary
+ * va_context on the group's first local device: every call that takes a context accepts it.
+ * A database sharded over the group holds rows [row0, row0 + rows) of the whole database on
+ * each rank (N / ranks rows each, the last rank also the remainder: va_shard_range), with global
+ * ids row0 + local row. va_knn_search, va_knn_search_host, va_int8_knn_search and
+ * va_hamming_knn_db over a sharded database search every shard exactly (each shard's own local
+ * top k, certified as on one device), exchange them in ONE ncclAllGather of packed 8-byte
+ * (value, id) records per rank and merge by (distance, id) on the front context's device, so the
+ * result equals the single-device search of the whole database. The communicators are
+ * non-blocking: NCCL steps and va_synchronize poll ncclCommGetAsyncError against the context's
+ * timeout and abort the communicators on expiry (VA_ERR_TIMEOUT) or error (VA_ERR_NCCL); an
+ * aborted group refuses further collectives. A sharded database is not grown in place. */
+#define VA_NCCL_ID_BYTES 128
+/* An NCCL unique id for va_context_create_rank (made by one rank, shared with the others out of
+ * band, e.g. through the launcher's store). */
+int va_nccl_unique_id(void* id);
+/* All listed devices in this process: one context and stream per device (cfg->stream, if set,
+ * belongs to devices[0]), one communicator per device. The returned context is devices[0]'s;
+ * queries and results of the sharded searches live there (queries reach the other devices by
+ * ncclBroadcast; each device's search runs in its own host thread). Destroying it destroys
+ * the group. */
+int va_context_create_multi(const int* devices, int ndev, const va_config* cfg, va_context** out);
+/* One rank of a group spread over processes (one process per GPU): cfg->device is this process's
+ * device, nranks the group size, rank this process's rank, nccl_id the shared unique id. Every
+ * rank calls it (NCCL initialisation is collective); the call waits, bounded by the timeout. */
+int va_context_create_rank(const va_config* cfg, int nranks, int rank, const void* nccl_id, va_context** out);
+/* Group size, the global rank of the context's first local device, and local devices (1, 0, 1
+ * for a single-device context). */
+int va_context_group(const va_context* ctx, int* nranks, int* rank, int* local_devices);
+/* Rows [row0, row0 + rows) of an n-row database that local device `member` holds. */
+int va_shard_range(const va_context* ctx, int64_t n, int member, int64_t* row0, int64_t* rows);
+/* Row-sharded databases. `rows` holds the rows this process owns, in global order: all n rows
+ * for a multi-device context, this rank's shard (va_shard_range) for a rank context; host memory
+ * (on_device = 0) or device memory (on_device = 1; for a multi-device context, on devices[0]).
+ * n is the row count of the WHOLE database. The int8 form codes every shard with the
+ * per-dimension range of the whole database (min / max all-reduced over the group). */
+int va_db_create_sharded(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype,
+                         va_database** out);
+int va_db_create_int8_sharded(va_context* ctx, const float* rows, int on_device, int64_t n, int dim,
+                              va_database** out);
+int va_db_create_binary_sharded(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
+                                va_database** out);
+/* The shard of local device `member` (a multi-device database), or the database itself (member 0
+ * of a rank's shard or of an unsharded database). */
+int va_db_shard(const va_database* db, int member, va_database** shard);
+
+/* ------------------------------------------------------------------------------------------ */
 /* Scalar quantization (ScalarQuantizationKernel, Kernels/Metal4/ScalarQuantizationKernel.swift;  */
 /* quantize_int8_kernel / dequantize_int8_kernel / int4, DataTransformations.metal:142-306)      */
 /* ------------------------------------------------------------------------------------------ */

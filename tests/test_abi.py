@@ -108,3 +108,10 @@ def test_binary_vector_helpers():
     a = va.Metal4BinaryVector(np.array([0b1100], np.uint32), 4)
     b = va.Metal4BinaryVector(np.array([0b1010], np.uint32), 4)
     assert a.hamming_distance(b) == 2 and a.bit(2) and not a.bit(0) and not a.bit(9)
+
+
+def test_nccl_unique_id_without_a_gpu():
+    # NCCL is loaded at run time; making a unique id needs no GPU
+    import vectoraccelerate_b200 as va
+    a, b = va.nccl_unique_id(), va.nccl_unique_id()
+    assert len(a) == 128 and a != b

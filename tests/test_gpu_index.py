@@ -49,3 +49,20 @@ def test_index_device_ingestion_matches_rebuild(ctx, oracle):
     got = idx.search_batch(q, 6)
     for r in range(5):
         assert [h.id.value for h in got[r].results] == [hs[live[i]].value for i in tids[r]]
+
+
+def test_index_filtered_search_past_the_device_selection_limit(ctx, oracle):
+    """A filter so selective that the doubling fetch passes 4,096 candidates: the remaining
+    candidates pass the filter first and the device search orders them (no host sort)."""
+    import vectoraccelerate_b200 as va
+    x = oracle.gen_gaussian(30_000, 32, 71)
+    idx = va.AcceleratedVectorIndex(va.IndexConfiguration.flat(32), ctx)
+    hs = idx.insert_batch(x, [{"tag": i % 7919 == 3} for i in range(30_000)])
+    q = oracle.gen_gaussian(2, 32, 72, row0=1 << 31)
+    tids, tvals = oracle.knn(q, x, 30_000)
+    for r in range(2):
+        got = idx.search(q[r], 3, filter=lambda h, m: m["tag"])
+        want = [int(i) for i in tids[r] if int(i) % 7919 == 3][:3]
+        assert [h.id.value for h in got.results] == [hs[i].value for i in want]
+        np.testing.assert_allclose([h.distance for h in got.results],
+                                   tvals[r][[list(tids[r]).index(i) for i in want]], rtol=1e-4)

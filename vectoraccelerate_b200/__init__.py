@@ -8,7 +8,7 @@ The compute lives in ``libva_cuda.so`` (hand-written CUDA for sm_100a behind the
 from . import _ffi
 from ._ffi import (DTYPE_BF16, DTYPE_F32, INVALID_ID, METRIC_COSINE, METRIC_IP, METRIC_L2SQ, PREC_AUTO, PREC_BF16,
                    PREC_FP32, PREC_TF32)
-from .context import DeviceBuffer, GPUContext, Metal4Configuration, Metal4Context
+from .context import DeviceBuffer, GPUContext, Metal4Configuration, Metal4Context, nccl_unique_id
 from .errors import (BufferAllocationFailed, CollectiveFailed, ComputeFailed, InvalidInput, Timeout, Unsupported,
                      VectorError)
 from .ivf import (IVFGPUIndexStructure, IVFSearchConfiguration, IVFSearchPipeline, IVFSearchResult,
@@ -18,8 +18,8 @@ from .provider import MetalComputeProvider
 from .kernels import (BinaryDatabase, BinaryQuantizationKernel, CosineSimilarityKernel, Database, DotProductKernel,
                       FusedL2TopKKernel, Int8Database, FusedL2TopKParameters, HammingDistanceKernel, L2DistanceKernel,
                       Metal4BinaryVector, Metal4FusedL2Config, Metal4FusedL2TopKResult, Metal4QuantizationResult,
-                      ScalarQuantizationKernel, TopKMergeKernel, TopKSelectionKernel, WarpOptimizedSelectionKernel,
-                      knn_search_host)
+                      ScalarQuantizationKernel, ShardedDatabase, TopKMergeKernel, TopKSelectionKernel,
+                      WarpOptimizedSelectionKernel, knn_search_host)
 
 # Type aliases of the reference (VectorAccelerate.swift:265-296).
 L2Kernel = L2DistanceKernel

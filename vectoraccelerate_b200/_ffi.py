@@ -22,6 +22,7 @@ PREC_AUTO, PREC_FP32, PREC_TF32, PREC_BF16 = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16 = 0, 1
 SELECT_MIN, SELECT_MAX = 0, 1
 MAX_DIM, MAX_K, MAX_SELECT_K = 4096, 1024, 4096
+NCCL_ID_BYTES = 128
 INVALID_ID = 0xFFFFFFFF
 
 _P = ctypes.c_void_p
@@ -75,6 +76,15 @@ SIGNATURES = {
     "va_knn_search_host": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_knn_search_noalloc": [_P, _P, _P, _I64, _I, _I, _I, _I, _P, _P],
     "va_last_search_stats": [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
+    "va_nccl_unique_id": [_P],
+    "va_context_create_multi": [_P, _I, ctypes.POINTER(VaConfig), _PP],
+    "va_context_create_rank": [ctypes.POINTER(VaConfig), _I, _I, _P, _PP],
+    "va_context_group": [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)],
+    "va_shard_range": [_P, _I64, _I, ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
+    "va_db_create_sharded": [_P, _P, _I, _I64, _I, _I, _PP],
+    "va_db_create_int8_sharded": [_P, _P, _I, _I64, _I, _PP],
+    "va_db_create_binary_sharded": [_P, _P, _I, _I64, _I, _PP],
+    "va_db_shard": [_P, _I, _PP],
     "va_sq_quantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_dequantize_int8": [_P, _P, _I64, _F, ctypes.c_int8, _P, _P, _I64, _P],
     "va_sq_quantize_int4": [_P, _P, _I64, _F, ctypes.c_int8, _P],

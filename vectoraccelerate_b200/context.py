@@ -87,6 +87,48 @@ class GPUContext:
         self.handle = h.value
         self.configuration = cfg
 
+    @classmethod
+    def multi(cls, devices, timeout_ms: int = 120_000, stream: int | None = None) -> "GPUContext":
+        """A group of devices in this process joined by an NCCL communicator
+        (va_context_create_multi); the context lives on devices[0]."""
+        devs = (ctypes.c_int * len(devices))(*devices)
+        c = _ffi.VaConfig(devices[0], timeout_ms, stream)
+        h = ctypes.c_void_p()
+        _ffi.call("va_context_create_multi", devs, len(devices), ctypes.byref(c), ctypes.byref(h))
+        self = cls.__new__(cls)
+        self.handle = h.value
+        self.configuration = Metal4Configuration(device=devices[0], timeout_ms=timeout_ms, stream=stream)
+        return self
+
+    @classmethod
+    def rank(cls, nranks: int, rank: int, nccl_id: bytes, configuration: Metal4Configuration | None = None
+             ) -> "GPUContext":
+        """One rank of a group spread over processes (va_context_create_rank); every rank calls it
+        with the same ``nccl_id`` (from ``nccl_unique_id()`` on one rank)."""
+        cfg = configuration or Metal4Configuration()
+        if len(nccl_id) != _ffi.NCCL_ID_BYTES:
+            raise InvalidInput(f"nccl_id must be {_ffi.NCCL_ID_BYTES} bytes, got {len(nccl_id)}")
+        c = _ffi.VaConfig(cfg.device, cfg.timeout_ms, cfg.stream)
+        h = ctypes.c_void_p()
+        idb = ctypes.create_string_buffer(bytes(nccl_id), _ffi.NCCL_ID_BYTES)
+        _ffi.call("va_context_create_rank", ctypes.byref(c), nranks, rank, idb, ctypes.byref(h))
+        self = cls.__new__(cls)
+        self.handle = h.value
+        self.configuration = cfg
+        return self
+
+    def group(self) -> tuple[int, int, int]:
+        """(ranks in the group, global rank of this context's first device, local devices)."""
+        a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _ffi.call("va_context_group", self.handle, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return a.value, b.value, c.value
+
+    def shard_range(self, n: int, member: int = 0) -> tuple[int, int]:
+        """(first row, rows) of an n-row database held by local device ``member``."""
+        r0, cnt = ctypes.c_int64(), ctypes.c_int64()
+        _ffi.call("va_shard_range", self.handle, n, member, ctypes.byref(r0), ctypes.byref(cnt))
+        return r0.value, cnt.value
+
     @property
     def device(self) -> int:
         return self.configuration.device
@@ -144,3 +186,10 @@ class GPUContext:
 
 
 Metal4Context = GPUContext
+
+
+def nccl_unique_id() -> bytes:
+    """An NCCL unique id (va_nccl_unique_id) for GPUContext.rank, shared by all ranks."""
+    buf = ctypes.create_string_buffer(_ffi.NCCL_ID_BYTES)
+    _ffi.call("va_nccl_unique_id", buf)
+    return buf.raw

@@ -10,15 +10,39 @@
 
 #include "va_internal.cuh"
 
+#include <nvtx3/nvToolsExt.h>
+
 static thread_local char g_last_error[1024] = "";
+
+int va_log_level() {
+    static const int level = [] {
+        const char* e = getenv("VA_LOG_LEVEL");
+        return e ? atoi(e) : 0;
+    }();
+    return level;
+}
 
 int va_set_error(int code, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
     vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
     va_end(ap);
+    if (va_log_level() >= 1) fprintf(stderr, "[libva_cuda] error %d: %s\n", code, g_last_error);
     return code;
 }
+
+void va_log_info(const char* fmt, ...) {
+    if (va_log_level() < 2) return;
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "[libva_cuda] %s\n", buf);
+}
+
+VaRange::VaRange(const char* name) { nvtxRangePushA(name); }
+VaRange::~VaRange() { nvtxRangePop(); }
 
 int va_check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
@@ -135,9 +159,11 @@ int va_context_create(const va_config* cfg, va_context** out) {
 
 int va_context_destroy(va_context* ctx) {
     if (!ctx) return VA_OK;
+    if (ctx->group) va_group_destroy(ctx);  // the group's other members and its communicators
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->gbuf) cudaFree(ctx->gbuf);
     if (ctx->io) cudaFree(ctx->io);
     if (ctx->aux) cudaFree(ctx->aux);
     if (ctx->d_error) cudaFree(ctx->d_error);
@@ -160,6 +186,15 @@ int va_context_stream(va_context* ctx, void** stream) {
 
 int va_synchronize(va_context* ctx) {
     VA_REQUIRE(ctx, "ctx must not be NULL");
+    if (ctx->group) return va_group_synchronize(ctx);
+    return va_sync_one(ctx);
+}
+
+}  // extern "C"
+
+// Bounded wait for this context's stream, then its device error word (the internal form: a
+// member of a group waits for its own work only).
+int va_sync_one(va_context* ctx) {
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     VA_CUDA_TRY(cudaEventRecord(ctx->ev_sync, ctx->stream));
     auto t0 = std::chrono::steady_clock::now();
@@ -180,6 +215,8 @@ int va_synchronize(va_context* ctx) {
     }
     return VA_OK;
 }
+
+extern "C" {
 
 int va_last_gpu_time_ms(va_context* ctx, float* ms) {
     VA_REQUIRE(ctx && ms, "ctx and ms must not be NULL");

@@ -218,6 +218,7 @@ extern "C" {
 
 int va_distance_matrix(va_context* ctx, const float* q, int64_t nq, const float* x, int64_t nx, int dim, int metric,
                        int flag, float* out, int64_t out_stride) {
+    VaRange nvtx_range("va_distance_matrix");
     VA_REQUIRE(ctx && q && x && out, "ctx, q, x and out must not be NULL");
     VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
     VA_REQUIRE(metric >= 0 && metric <= 2, "metric must be 0 (L2SQ), 1 (COSINE) or 2 (IP), got %d", metric);

@@ -128,6 +128,7 @@ extern "C" {
 
 int va_db_append(va_context* ctx, va_database* db, const void* rows, int on_device, int64_t count) {
     VA_REQUIRE(ctx && db && rows, "ctx, db and rows must not be NULL");
+    VA_REQUIRE(!va_is_sharded(db), "a sharded database is not grown, updated or compacted in place (rebuild it)");
     VA_REQUIRE(count >= 0, "count must be >= 0, got %lld", (long long)count);
     VA_REQUIRE(db->ctx->device == ctx->device, "database lives on device %d, context on device %d", db->ctx->device,
                ctx->device);
@@ -146,6 +147,7 @@ int va_db_append(va_context* ctx, va_database* db, const void* rows, int on_devi
 
 int va_db_update(va_context* ctx, va_database* db, int64_t slot0, const void* rows, int on_device, int64_t count) {
     VA_REQUIRE(ctx && db && rows, "ctx, db and rows must not be NULL");
+    VA_REQUIRE(!va_is_sharded(db), "a sharded database is not grown, updated or compacted in place (rebuild it)");
     VA_REQUIRE(slot0 >= 0 && count >= 0 && slot0 + count <= db->n,
                "slots [%lld, %lld) outside the database's %lld rows", (long long)slot0, (long long)(slot0 + count),
                (long long)db->n);
@@ -159,6 +161,7 @@ int va_db_update(va_context* ctx, va_database* db, int64_t slot0, const void* ro
 
 int va_db_compact(va_context* ctx, va_database* db, const uint8_t* keep, int64_t* new_slot) {
     VA_REQUIRE(ctx && db && keep, "ctx, db and keep must not be NULL");
+    VA_REQUIRE(!va_is_sharded(db), "a sharded database is not grown, updated or compacted in place (rebuild it)");
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     const int64_t n = db->n;
     std::vector<int64_t> kept;

@@ -404,7 +404,7 @@ int int8_fallback(va_context* ctx, va_database* db, const float* queries, int k,
                   const uint32_t* fail_cnt, float* gq, float* gv, uint32_t* gi, float* out_vals, uint32_t* out_ids) {
     uint32_t nf = 0;
     VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_TRY(va_synchronize(ctx));
+    VA_TRY(va_sync_one(ctx));
     if (!nf) return VA_OK;
     const int dim = db->dim, cpad = db->cpad;
     const int64_t n = db->n;
@@ -560,6 +560,7 @@ int va_sq_perdim_minmax(va_context* ctx, const float* x, int64_t n, int dim, flo
 
 int va_db_create_int8(va_context* ctx, const float* rows, int on_device, int64_t n, int dim, const float* mins,
                       const float* maxs, uint32_t id_base, va_database** out) {
+    VaRange nvtx_range("va_db_create_int8");
     VA_REQUIRE(ctx && rows && out, "ctx, rows and out must not be NULL");
     VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
     VA_REQUIRE(dim > 0, "dimension must be positive, got %d", dim);
@@ -617,6 +618,16 @@ int va_db_int8_params(const va_database* db, const float** mins, const float** s
 
 int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int candidates,
                        float* out_vals, uint32_t* out_ids) {
+    VaRange nvtx_range("va_int8_knn_search");
+    VA_REQUIRE(ctx && cdb && queries && out_vals && out_ids, "all pointers must be non-NULL");
+    if (va_is_sharded(cdb)) return va_sharded_int8(ctx, cdb, queries, nq, k, candidates, out_vals, out_ids);
+    return va_int8_knn_local(ctx, cdb, queries, nq, k, candidates, out_vals, out_ids);
+}
+
+}  // extern "C"
+
+int va_int8_knn_local(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int candidates,
+                      float* out_vals, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && queries && out_vals && out_ids, "all pointers must be non-NULL");
     VA_REQUIRE(cdb->kind == VA_DB_INT8, "database is not an int8 database (use va_db_create_int8)");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
@@ -664,8 +675,11 @@ int va_int8_knn_search(va_context* ctx, const va_database* cdb, const float* que
     return int8_fallback(ctx, db, queries, k, candidates, fail_list, fail_cnt, gq, gv, gi, out_vals, out_ids);
 }
 
+extern "C" {
+
 int va_db_create_binary(va_context* ctx, const uint32_t* codes, int on_device, int64_t n, int dim_bits,
                         uint32_t id_base, va_database** out) {
+    VaRange nvtx_range("va_db_create_binary");
     VA_REQUIRE(ctx && codes && out, "ctx, codes and out must not be NULL");
     VA_REQUIRE(n > 0, "numDataset must be positive, got %lld", (long long)n);
     VA_REQUIRE(dim_bits > 0 && dim_bits <= 8192, "dimension must be in 1..8192 bits, got %d", dim_bits);
@@ -711,6 +725,16 @@ int va_db_binary_set_chunk_rows(va_database* db, int64_t rows) {
 
 int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* queries, int64_t nq, int k,
                       uint32_t* out_dists, uint32_t* out_ids) {
+    VaRange nvtx_range("va_hamming_knn_db");
+    VA_REQUIRE(ctx && cdb && queries && out_ids, "ctx, db, queries and out_ids must not be NULL");
+    if (va_is_sharded(cdb)) return va_sharded_hamming(ctx, cdb, queries, nq, k, out_dists, out_ids);
+    return va_hamming_knn_local(ctx, cdb, queries, nq, k, out_dists, out_ids);
+}
+
+}  // extern "C"
+
+int va_hamming_knn_local(va_context* ctx, const va_database* cdb, const uint32_t* queries, int64_t nq, int k,
+                         uint32_t* out_dists, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && queries && out_ids, "ctx, db, queries and out_ids must not be NULL");
     VA_REQUIRE(cdb->kind == VA_DB_BINARY, "database is not a binary database (use va_db_create_binary)");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
@@ -810,5 +834,3 @@ int va_hamming_knn_db(va_context* ctx, const va_database* cdb, const uint32_t* q
     if (db->id_base) k_add_base_ids<<<blocks, 256, 0, ctx->stream>>>(out_ids, nq * k, db->id_base);
     return va_check_launch("k_bits_to_dists");
 }
-
-}  // extern "C"

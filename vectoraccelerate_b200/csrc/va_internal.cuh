@@ -15,6 +15,18 @@
 // ------------------------------------------------------------------------------------------------
 int va_set_error(int code, const char* fmt, ...);
 
+// Diagnostics (the reference's Logger, Core/Logger.swift:71, as an environment switch):
+// VA_LOG_LEVEL=1 prints every error status with its message to stderr, 2 also prints
+// informational lines (group set-up, per-search certificate counts). Off by default.
+int va_log_level();
+void va_log_info(const char* fmt, ...);
+
+// NVTX range around a public entry point (visible in Nsight Systems / Compute; free otherwise).
+struct VaRange {
+    explicit VaRange(const char* name);
+    ~VaRange();
+};
+
 #define VA_CUDA_TRY(expr)                                                                          \
     do {                                                                                           \
         cudaError_t _e = (expr);                                                                   \
@@ -66,7 +78,19 @@ struct va_context {
     // and queries that took the exact route.
     int64_t stat_uncertified = 0;
     int64_t stat_exact = 0;
+    // Multi-GPU (va_group.cu): set on the front context of a group only (a process-per-GPU rank
+    // context, or the first device of a multi-device context); member contexts stay plain.
+    struct va_group* group = nullptr;
+    // Scratch of the sharded search's exchange (local lists, gathered records, merge inputs).
+    void* gbuf = nullptr;
+    size_t gbuf_bytes = 0;
 };
+
+// Bounded wait for one context's own stream and device error word (internal waits of a search).
+int va_sync_one(va_context* ctx);
+// Group synchronisation and NCCL error polling behind va_synchronize (va_group.cu).
+int va_group_synchronize(va_context* ctx);
+void va_group_destroy(va_context* ctx);
 
 // Device staging buffer of at least `bytes` for host-buffer calls.
 int va_io_buffer(va_context* ctx, size_t bytes, void** out);
@@ -114,7 +138,30 @@ struct va_database {
     // `kind` (VA_CERT_*). Maxima only grow (a compaction keeps them: still valid upper bounds).
     uint32_t* cert = nullptr;
     unsigned cert_ready = 0;     // bit kind set once cert[1 + kind] covers every row
+    // Row-sharded database (va_group.cu): a multi-device context's database holds one shard per
+    // device in `shards` (this object then holds no rows); a rank context's database is its own
+    // shard with `group_shard` set. n_total = rows of the whole database.
+    va_database** shards = nullptr;
+    int nshards = 0;
+    bool group_shard = false;
+    int64_t n_total = 0;
 };
+
+// True when a search over db runs per shard and merges across the group.
+inline bool va_is_sharded(const va_database* db) { return db->shards != nullptr || db->group_shard; }
+int va_sharded_knn(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int metric,
+                   int precision, int rerank, float* out_vals, uint32_t* out_ids);
+int va_sharded_int8(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int candidates,
+                    float* out_vals, uint32_t* out_ids);
+int va_sharded_hamming(va_context* ctx, const va_database* db, const uint32_t* queries, int64_t nq, int k,
+                       uint32_t* out_dists, uint32_t* out_ids);
+// Plain (one-device) searches, called per shard by the sharded ones.
+int va_knn_search_local(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int metric,
+                        int precision, int rerank, float* out_vals, uint32_t* out_ids);
+int va_int8_knn_local(va_context* ctx, const va_database* db, const float* queries, int64_t nq, int k, int candidates,
+                      float* out_vals, uint32_t* out_ids);
+int va_hamming_knn_local(va_context* ctx, const va_database* db, const uint32_t* queries, int64_t nq, int k,
+                         uint32_t* out_dists, uint32_t* out_ids);
 
 // Operand kinds of the certificate (which reduced-precision copy of a row the filter reads).
 #define VA_CERT_BF16 0     // bf16(x)

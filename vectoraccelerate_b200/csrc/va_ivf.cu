@@ -510,6 +510,7 @@ extern "C" {
 
 int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist, int max_iters, float tol,
                  uint64_t seed, int init, float* out_centroids, int* out_iters) {
+    VaRange nvtx_range("va_ivf_train");
     VA_REQUIRE(ctx && x && out_centroids, "ctx, x and out_centroids must not be NULL");
     VA_REQUIRE(dim > 0 && dim <= VA_MAX_DIM, "dimension must be in 1..%d, got %d", VA_MAX_DIM, dim);
     VA_REQUIRE(nlist > 0 && nlist <= n, "nlist must be in 1..numVectors (%lld), got %d", (long long)n, nlist);
@@ -608,6 +609,7 @@ int va_ivf_train(va_context* ctx, const float* x, int64_t n, int dim, int nlist,
 
 int va_ivf_create(va_context* ctx, const float* rows, int64_t n, int dim, const float* centroids, int nlist,
                   uint32_t id_base, va_ivf** out) {
+    VaRange nvtx_range("va_ivf_create");
     VA_REQUIRE(ctx && rows && centroids && out, "ctx, rows, centroids and out must not be NULL");
     VA_REQUIRE(n > 0 && dim > 0 && dim <= VA_MAX_DIM && nlist > 0, "n, dim (<= %d) and nlist must be positive",
                VA_MAX_DIM);
@@ -776,6 +778,7 @@ int va_ivf_list_sizes(const va_ivf* ivf, int64_t* sizes) {
 
 int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int64_t nq, int k, int nprobe,
                   float* out_vals, uint32_t* out_ids) {
+    VaRange nvtx_range("va_ivf_search");
     VA_REQUIRE(ctx && civf && queries && out_vals && out_ids, "all pointers must be non-NULL");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(k > 0 && k <= 128, "k must be between 1 and 128 for the IVF search, got %d", k);

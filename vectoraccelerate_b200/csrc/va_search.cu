@@ -522,7 +522,7 @@ int scatter_results(va_context* ctx, const float* v, const uint32_t* ids, const 
 // Count written by a merge (the call waits for the stream: the next passes depend on it).
 int read_count(va_context* ctx, const uint32_t* dcnt, uint32_t* n) {
     VA_CUDA_TRY(cudaMemcpyAsync(n, dcnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    return va_synchronize(ctx);
+    return va_sync_one(ctx);
 }
 
 // Exact route: the reference's chunked two-pass strategy (executeChunkedTwoPass,
@@ -682,6 +682,7 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     uint32_t n1 = 0;
     VA_TRY(read_count(ctx, cnt, &n1));
     ctx->stat_uncertified = n1;
+    va_log_info("va_knn_search: %lld queries, pool %d: %u not certified by the first pass", (long long)nq, pool, n1);
     if (!n1) return VA_OK;
     VA_TRY(gather_queries(ctx, queries, db->dim, list1, n1, gq1));
     const int pool2 = wider_pool(pool);
@@ -812,11 +813,18 @@ extern "C" {
 
 int va_db_create(va_context* ctx, const void* rows, int on_device, int64_t n, int dim, int dtype, uint32_t id_base,
                  va_database** out) {
+    VaRange nvtx_range("va_db_create");
     return db_create_impl(ctx, rows, on_device, n, dim, dtype, id_base, out, true);
 }
 
 int va_db_destroy(va_database* db) {
     if (!db) return VA_OK;
+    if (db->shards) {
+        for (int m = 0; m < db->nshards; ++m) va_db_destroy(db->shards[m]);
+        delete[] db->shards;
+        delete db;
+        return VA_OK;
+    }
     cudaSetDevice(db->ctx->device);
     cudaStreamSynchronize(db->ctx->stream);
     if (db->op && !db->op_alias) cudaFree(db->op);
@@ -839,7 +847,7 @@ int va_db_destroy(va_database* db) {
 
 int va_db_info(const va_database* db, int64_t* n, int* dim, int* dtype) {
     VA_REQUIRE(db, "db must not be NULL");
-    if (n) *n = db->n;
+    if (n) *n = va_is_sharded(db) ? db->n_total : db->n;
     if (dim) *dim = db->dim;
     if (dtype) *dtype = db->dtype;
     return VA_OK;
@@ -847,12 +855,24 @@ int va_db_info(const va_database* db, int64_t* n, int* dim, int* dtype) {
 
 int va_db_rows(const va_database* db, const void** rows) {
     VA_REQUIRE(db && rows, "db and rows must not be NULL");
+    VA_REQUIRE(!db->shards, "a multi-device sharded database has one row array per device (va_db_shard)");
     *rows = db->rows;
     return VA_OK;
 }
 
 int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int metric,
                   int precision, int rerank, float* out_vals, uint32_t* out_ids) {
+    VaRange nvtx_range("va_knn_search");
+    VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
+    if (va_is_sharded(cdb))
+        return va_sharded_knn(ctx, cdb, queries, nq, k, metric, precision, rerank, out_vals, out_ids);
+    return va_knn_search_local(ctx, cdb, queries, nq, k, metric, precision, rerank, out_vals, out_ids);
+}
+
+}  // extern "C"
+
+int va_knn_search_local(va_context* ctx, const va_database* cdb, const float* queries, int64_t nq, int k, int metric,
+                        int precision, int rerank, float* out_vals, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
     VA_REQUIRE(cdb->kind != VA_DB_BINARY, "a binary database is searched with va_hamming_knn_db");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
@@ -883,6 +903,8 @@ int va_knn_search(va_context* ctx, const va_database* cdb, const float* queries,
     return VA_OK;
 }
 
+extern "C" {
+
 int va_last_search_stats(va_context* ctx, int64_t* uncertified, int64_t* exact) {
     VA_REQUIRE(ctx && uncertified && exact, "ctx, uncertified and exact must not be NULL");
     *uncertified = ctx->stat_uncertified;
@@ -892,10 +914,12 @@ int va_last_search_stats(va_context* ctx, int64_t* uncertified, int64_t* exact) 
 
 int va_knn_search_host(va_context* ctx, const va_database* db, const float* queries_host, int64_t nq, int k,
                        int metric, int precision, int rerank, float* out_vals_host, uint32_t* out_ids_host) {
+    VaRange nvtx_range("va_knn_search_host");
     VA_REQUIRE(ctx && db && queries_host && out_vals_host && out_ids_host, "all pointers must be non-NULL");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(k > 0, "k must be positive, got %d", k);
     VA_REQUIRE(k <= VA_MAX_K, "k %d exceeds maximum supported k %d", k, VA_MAX_K);
+    VA_REQUIRE(db->kind != VA_DB_BINARY, "a binary database is searched with va_hamming_knn_db");
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
     const size_t qb = (size_t)nq * db->dim * 4, rb = (size_t)nq * k * 4;
     void* io;
@@ -1036,6 +1060,7 @@ extern "C" int va_knn_search_noalloc(va_context* ctx, const va_database* cdb, co
                                      int metric, int precision, int rerank, float* out_vals, uint32_t* out_ids) {
     VA_REQUIRE(ctx && cdb && out_vals && out_ids, "ctx, db, out_vals and out_ids must not be NULL");
     VA_REQUIRE(cdb->kind != VA_DB_BINARY, "a binary database is searched with va_hamming_knn_db");
+    VA_REQUIRE(!va_is_sharded(cdb), "the allocation-free search takes a single-device database, not a sharded one");
     VA_REQUIRE(nq > 0, "numQueries must be positive, got %lld", (long long)nq);
     VA_REQUIRE(queries, "queries must not be NULL");
     VA_REQUIRE(k > 0, "k must be positive, got %d", k);

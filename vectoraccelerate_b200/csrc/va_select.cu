@@ -110,6 +110,7 @@ extern "C" {
 
 int va_topk_select(va_context* ctx, const float* in, int64_t batch, int64_t n, int64_t in_stride, int k, int mode,
                    float* out_vals, uint32_t* out_ids, int64_t out_stride) {
+    VaRange nvtx_range("va_topk_select");
     VA_REQUIRE(ctx && in, "ctx and in must not be NULL");
     VA_REQUIRE(out_vals || out_ids, "at least one of out_vals / out_ids is required");
     VA_REQUIRE(k > 0 && k <= VA_MAX_SELECT_K, "k must be between 1 and %d, got %d", VA_MAX_SELECT_K, k);
@@ -164,6 +165,7 @@ int va_merge_lists_internal(va_context* ctx, const float* vals, const uint32_t* 
 
 int va_merge_shards(va_context* ctx, const float* vals, const uint32_t* ids, int nshards, int64_t nq, int k, int mode,
                     float* out_vals, uint32_t* out_ids) {
+    VaRange nvtx_range("va_merge_shards");
     VA_REQUIRE(ctx && vals && ids && out_vals && out_ids, "all buffers must be non-NULL");
     VA_REQUIRE(nshards > 0, "nshards must be positive, got %d", nshards);
     VA_REQUIRE(k > 0 && k <= VA_MAX_SELECT_K, "k must be between 1 and %d, got %d", VA_MAX_SELECT_K, k);

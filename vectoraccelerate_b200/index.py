@@ -111,8 +111,11 @@ class AcceleratedVectorIndex:
         self.configuration = configuration
         self.context = context or GPUContext()
         self.precision = precision
-        self._rows = np.zeros((0, configuration.dimension), np.float32)
-        self._deleted = np.zeros(0, bool)
+        # Host copy of the rows in preallocated capacity that grows geometrically (as the device
+        # storage does, GPUVectorStorage.swift:75-260), so inserts are amortized O(rows written).
+        self._row_buf = np.zeros((0, configuration.dimension), np.float32)
+        self._del_buf = np.zeros(0, bool)
+        self._n = 0
         self._slot_handle: list[int] = []          # slot -> handle value
         self._handle_slot: dict[int, int] = {}     # live handle value -> slot
         self._metadata: dict[int, VectorMetadata] = {}
@@ -123,6 +126,30 @@ class AcceleratedVectorIndex:
         self._ivf = None
         self._ivf_dirty = True
         self._auto_train = True
+
+    # ------------------------------------------------------------------------- storage
+    @property
+    def _rows(self) -> np.ndarray:
+        return self._row_buf[:self._n]
+
+    @property
+    def _deleted(self) -> np.ndarray:
+        return self._del_buf[:self._n]
+
+    def _append_rows(self, v: np.ndarray) -> int:
+        """Write rows after the last slot (capacity at least doubles when full); returns the first slot."""
+        slot0, need = self._n, self._n + v.shape[0]
+        if need > self._row_buf.shape[0]:
+            cap = max(need, 2 * self._row_buf.shape[0], 256)
+            rows = np.zeros((cap, self.configuration.dimension), np.float32)
+            rows[:slot0] = self._row_buf[:slot0]
+            dele = np.zeros(cap, bool)
+            dele[:slot0] = self._del_buf[:slot0]
+            self._row_buf, self._del_buf = rows, dele
+        self._row_buf[slot0:need] = v
+        self._del_buf[slot0:need] = False
+        self._n = need
+        return slot0
 
     # ------------------------------------------------------------------------- mutation
     def insert(self, vector, metadata: Optional[VectorMetadata] = None) -> VectorHandle:
@@ -136,9 +163,7 @@ class AcceleratedVectorIndex:
             raise VAIndexError(f"dimension mismatch: expected {self.configuration.dimension}, got {v.shape[1]}")
         if metadata is not None and len(metadata) != v.shape[0]:
             raise VAIndexError(f"metadata count {len(metadata)} != vector count {v.shape[0]}")
-        slot0 = self._rows.shape[0]
-        self._rows = np.concatenate([self._rows, v])
-        self._deleted = np.concatenate([self._deleted, np.zeros(v.shape[0], bool)])
+        slot0 = self._append_rows(v)
         handles = []
         for i in range(v.shape[0]):
             h = self._next_handle
@@ -187,10 +212,11 @@ class AcceleratedVectorIndex:
                 self._db.close()
                 self._db = None
         self._ivf_dirty = True
-        self._rows = np.ascontiguousarray(self._rows[keep])
+        kept = np.ascontiguousarray(self._rows[keep])
+        self._n = 0
+        self._append_rows(kept)
         self._slot_handle = [h for h, k in zip(self._slot_handle, keep) if k]
         self._handle_slot = {h: s for s, h in enumerate(self._slot_handle)}
-        self._deleted = np.zeros(self._rows.shape[0], bool)
 
     def set_metadata(self, metadata: Optional[VectorMetadata], handle: VectorHandle) -> None:
         if handle.value not in self._handle_slot:
@@ -301,21 +327,45 @@ class AcceleratedVectorIndex:
         return self._db
 
     def _fetch(self, q: np.ndarray, fetch_k: int):
-        """(values, slots) of the fetch_k best slots per query row, best first, (value, slot)
-        order: the fused search up to its k limit (1024), beyond it the device distance matrix
-        and the device top-k selection (up to 4096); past that (a filtered search that has
-        examined 4096 candidates without finding k) the device-computed distance row is ordered
-        on the host."""
+        """(values, slots) of the fetch_k (<= 4096) best slots per query row, best first, (value,
+        slot) order: the fused search up to its k limit (1024), beyond it the device distance
+        matrix and the device top-k selection."""
         from .kernels import MAXIMUM, MINIMUM, TopKSelectionKernel, _matrix
         metric = _METRICS[self.configuration.metric]
         if fetch_k <= _ffi.MAX_K:
             return knn_search_host(self.context, self._database(), q, fetch_k, metric, self.precision)
         m = _matrix(self.context, q, self._rows, metric, metric == _ffi.METRIC_COSINE)
         larger = metric == _ffi.METRIC_IP
-        if fetch_k <= _ffi.MAX_SELECT_K:
-            return TopKSelectionKernel(self.context).select_arrays(m, fetch_k, MAXIMUM if larger else MINIMUM)
-        order = np.argsort(-m if larger else m, axis=1, kind="stable")[:, :fetch_k]
-        return np.take_along_axis(m, order, 1).astype(np.float32), order.astype(np.uint32)
+        return TopKSelectionKernel(self.context).select_arrays(m, fetch_k, MAXIMUM if larger else MINIMUM)
+
+    def _search_survivors(self, q: np.ndarray, k: int, filter: Filter, seen: set) -> list:  # noqa: A002
+        """The filtered search's last step once the doubling fetch passes 4096 candidates (a very
+        selective filter): the filter runs over every live slot not examined yet, and the exact
+        device search runs over the rows that pass (a temporary database of those rows; ids map
+        back to slots)."""
+        live = np.nonzero(~self._deleted)[0]
+        keep = []
+        for s in live:
+            if int(s) in seen:
+                continue
+            h = VectorHandle(self._slot_handle[int(s)])
+            if filter(h, self._metadata.get(h.value)):
+                keep.append(int(s))
+        if not keep:
+            return []
+        slots = np.asarray(keep, np.int64)
+        sub = Database(self.context, self._rows[slots])
+        try:
+            metric = _METRICS[self.configuration.metric]
+            vals, ids = knn_search_host(self.context, sub, q, min(k, len(keep), _ffi.MAX_K), metric, self.precision)
+        finally:
+            sub.close()
+        out = []
+        for i, v in zip(ids[0], vals[0]):
+            if int(i) != _ffi.INVALID_ID:
+                s = int(slots[int(i)])
+                out.append(IndexSearchResult(VectorHandle(self._slot_handle[s]), float(v)))
+        return out
 
     def search(self, query, k: int, filter: Optional[Filter] = None) -> SearchResults:  # noqa: A002
         q = np.ascontiguousarray(query, np.float32)
@@ -397,5 +447,9 @@ class AcceleratedVectorIndex:
             nxt = min(fetch_k * 2, allocated)
             if nxt == fetch_k or len(seen) >= allocated:
                 break
+            if nxt > _ffi.MAX_SELECT_K:
+                # every later candidate passes the filter first; the device search orders them
+                results.extend(self._search_survivors(q, k - len(results), filter, seen))
+                return SearchResults(results[:k], candidates_searched=allocated, is_exhaustive=True)
             fetch_k = nxt
         return SearchResults(results, candidates_searched=len(seen), is_exhaustive=True)

@@ -658,3 +658,45 @@ class BinaryDatabase(_DbHandle):
         oi = ctx.get_buffer(4 * q.shape[0] * k, np.uint32, (q.shape[0], k))
         _ffi.call("va_hamming_knn_db", ctx.handle, self.handle, dq.ptr, q.shape[0], k, od.ptr, oi.ptr)
         return od.download(), oi.download()
+
+
+class ShardedDatabase(_DbHandle):
+    """A row-sharded database over a group context (va_db_create_sharded, _int8_sharded,
+    _binary_sharded): each rank holds rows [row0, row0 + rows) of the n-row database
+    (``GPUContext.shard_range``). ``rows`` are the rows this process owns, in global order: all
+    n rows for a multi-device context, this rank's shard for a rank context; a numpy array, or a
+    device pointer with ``device_ptr``. Searched with the usual entry points (va_knn_search,
+    va_int8_knn_search, va_hamming_knn_db), whose results are the whole database's."""
+
+    def __init__(self, context: GPUContext, rows=None, n: int | None = None, dim: int | None = None,
+                 kind: str = "float", dtype: int = _ffi.DTYPE_F32, device_ptr: int | None = None):
+        self.context = context
+        self.kind = kind
+        if device_ptr is None:
+            np_dt = np.uint32 if kind == "binary" else (np.uint16 if dtype == _ffi.DTYPE_BF16 else np.float32)
+            a = np.ascontiguousarray(rows, dtype=np_dt)
+            ptr, on_dev = a.ctypes.data_as(_vp), 0
+            dim = dim or (a.shape[1] * 32 if kind == "binary" else a.shape[1])
+            n = n or a.shape[0]
+        else:
+            ptr, on_dev = device_ptr, 1
+        h = ctypes.c_void_p()
+        if kind == "float":
+            _ffi.call("va_db_create_sharded", context.handle, ptr, on_dev, n, dim, dtype, ctypes.byref(h))
+        elif kind == "int8":
+            _ffi.call("va_db_create_int8_sharded", context.handle, ptr, on_dev, n, dim, ctypes.byref(h))
+        elif kind == "binary":
+            _ffi.call("va_db_create_binary_sharded", context.handle, ptr, on_dev, n, dim, ctypes.byref(h))
+        else:
+            raise InvalidInput(f"kind must be float, int8 or binary, got {kind!r}")
+        context.synchronize()
+        self.handle = h.value
+        self.n, self.dim, self.dtype = n, dim, dtype
+
+    def rows_ptr(self, member: int = 0) -> int:
+        """Device pointer of local device ``member``'s shard rows (codes for a binary database)."""
+        sh = ctypes.c_void_p()
+        _ffi.call("va_db_shard", self.handle, member, ctypes.byref(sh))
+        p = ctypes.c_void_p()
+        _ffi.call("va_db_rows", sh.value, ctypes.byref(p))
+        return p.value

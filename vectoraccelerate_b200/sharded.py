@@ -1,14 +1,15 @@
-"""Row-sharded flat search across GPUs of one node (one process per GPU).
+"""Row-sharded flat search across GPUs of one node.
 
-The reference is single-GPU; this is the build's multi-GPU layer for the same search. Each rank
-holds rows [row0, row0 + n_local) of the database (``shard_bounds``) with global ids
-row0 + local row, searches them exactly, and the per-rank top-k lists are all-gathered
-(torch.distributed: NCCL on GPUs, gloo on CPU) and merged with the (distance, id) order. Every
-rank's list is already exact, so the merged list is exact.
+The product path is the C ABI: ``GPUContext.rank`` (va_context_create_rank, one process per GPU)
+or ``GPUContext.multi`` (va_context_create_multi, every device in one process) with a
+``ShardedDatabase`` (va_db_create_sharded): every library search then searches each shard,
+exchanges the per-shard top-k lists in one NCCL all-gather of packed (value, id) records and
+merges them on the device. The reference is single-GPU; this is the build's multi-GPU layer.
 
-``local_search`` and ``merge`` are injectable so the gather logic runs on CPU in tests; the
-defaults call libva_cuda (``va_knn_search`` on the shard, ``va_merge_shards`` on the gathered
-lists).
+This module keeps the shard arithmetic (``shard_bounds``, the same split as va_shard_range) and a
+restatement of the exchange over torch.distributed (``ShardedSearch``: all-gather, then merge by
+(distance, id)) whose ``local_search`` and ``merge`` are injectable, so the gather logic runs on
+CPU with gloo in tests; ``merge_lists_host`` is its reference merge.
 """
 
 from __future__ import annotations
