@@ -20,7 +20,7 @@ def _near_duplicate_db(n, d, dup, seed, spread=1e-3, normalize=False):
     near that query (the query's top k lie inside the run)."""
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((n, d)).astype(np.float32)
-    q = rng.standard_normal((16, d)).astype(np.float32)
+    q = rng.standard_normal((64, d)).astype(np.float32)
     runs = []
     for i in range(4):
         p = q[i] + 0.5 * rng.standard_normal(d).astype(np.float32)
@@ -85,3 +85,27 @@ def test_wide_pool_certificate(ctx, oracle):
     vals, ids, (unc, exact) = _search(ctx, x, q, 60)
     assert unc >= 4
     _check(oracle, q, x, 60, 0, vals, ids)
+
+
+def test_dense_neighbourhoods_widen_the_pool_and_are_remembered(ctx, oracle):
+    # Every query sits next to its own run of 200 near-duplicates: the whole batch fails the first
+    # pool (32), the second pass takes a pool of 512 (more than the run), and the database keeps
+    # that pool for its next searches of the metric, which then certify in their first pass.
+    import vectoraccelerate_b200 as va
+    rng = np.random.default_rng(21)
+    q = rng.standard_normal((80, 96)).astype(np.float32)
+    runs = [q[i] + 0.5 * rng.standard_normal(96).astype(np.float32) for i in range(80)]
+    x = np.concatenate([rng.standard_normal((10_000, 96)).astype(np.float32)] +
+                       [p[None, :] + 1e-3 * rng.standard_normal((200, 96)).astype(np.float32) for p in runs])
+    x = np.ascontiguousarray(x[rng.permutation(len(x))])  # a run's rows spread over the row splits
+    db = va.Database(ctx, x)
+    try:
+        vals, ids = va.knn_search_host(ctx, db, q, 10, 0, va.PREC_BF16)
+        unc, exact = ctx.last_search_stats()
+        assert unc == 80 and exact == 0, (unc, exact)
+        _check(oracle, q, x, 10, 0, vals, ids)
+        vals, ids = va.knn_search_host(ctx, db, q, 10, 0, va.PREC_BF16)
+        assert ctx.last_search_stats() == (0, 0)
+        _check(oracle, q, x, 10, 0, vals, ids)
+    finally:
+        db.close()

@@ -192,3 +192,29 @@ def test_kmeanspp_seeds(ctx, oracle):
     assert len(set(rows)) == 8 and sorted(set(lab[rows])) == list(range(8))
     km = va.KMeansPipeline(ctx, va.KMeansConfiguration(num_clusters=8, dimension=16, max_iterations=20)).fit(x)
     assert km.converged and len(set(km.assignments[lab == 0])) == 1
+
+
+@pytest.mark.parametrize("k", [10, 60])
+def test_ivf_certificate_rescans_near_duplicates(ctx, oracle, k):
+    """Runs of near-duplicate rows inside a list defeat the list scan's certificate: those queries
+    are rescanned exactly and the result still equals the oracle's (exact within the probes)."""
+    import vectoraccelerate_b200 as va
+    from oracle import ivf as O
+    from conftest import assert_knn_parity
+    rng = np.random.default_rng(5 + k)
+    x = rng.standard_normal((20_000, 64)).astype(np.float32)
+    q = rng.standard_normal((12, 64)).astype(np.float32)
+    runs = [q[i] + 0.3 * rng.standard_normal(64).astype(np.float32) for i in range(4)]
+    dup = np.concatenate([p[None, :] + 1e-3 * rng.standard_normal((300, 64)).astype(np.float32) for p in runs])
+    x = np.concatenate([x, dup]).astype(np.float32)
+    cent = x[::1000][:16].copy()
+    pipe = va.IVFSearchPipeline(ctx, va.IVFSearchConfiguration(16, 4, 64))
+    st = pipe.build(x, cent)
+    try:
+        rows, ids, offs = O.build_lists(x, cent)
+        res = pipe.search(q, st, k)
+        assert ctx.last_search_stats()[0] >= 1
+        tv, ti = O.search(q, cent, rows, ids, offs, k, 4)
+        assert_knn_parity(res.indices, res.distances, ti, tv, _true_vals(q, x, res.indices))
+    finally:
+        st.close()

@@ -138,6 +138,9 @@ struct va_database {
     // `kind` (VA_CERT_*). Maxima only grow (a compaction keeps them: still valid upper bounds).
     uint32_t* cert = nullptr;
     unsigned cert_ready = 0;     // bit kind set once cert[1 + kind] covers every row
+    // Learned per metric: candidate pool of later tensor-core searches, as a multiple of k, once a
+    // batch showed neighbourhoods too dense for the first pool to certify (0: no hint).
+    int pool_hint[3] = {0, 0, 0};
     // Row-sharded database (va_group.cu): a multi-device context's database holds one shard per
     // device in `shards` (this object then holds no rows); a rank context's database is its own
     // shard with `group_shard` set. n_total = rows of the whole database.

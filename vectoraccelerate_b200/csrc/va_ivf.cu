@@ -55,6 +55,9 @@ struct va_ivf {
     size_t scratch_bytes = 0;
     int* h_plan = nullptr;
     size_t h_plan_ints = 0;
+    // Certificate inputs of the list scan (as a flat database's, va_internal.cuh): max |x| and the
+    // max operand error of the bf16 and the tf32 operands over the rows.
+    uint32_t* cert = nullptr;
 };
 
 namespace {
@@ -238,6 +241,52 @@ __global__ void k_row_norms(const float* __restrict__ x, int64_t n, int dim, int
     if (lane == 0) bias[r] = (float)s;
 }
 
+// Certificate inputs over the rows: cert[0] = max |x|, cert[1 + kind] = max |operand - x| for the
+// bf16 and tf32 operands (rounded up). A warp per row.
+__global__ void k_ivf_row_cert(const float* __restrict__ x, int64_t n, int dim, uint32_t* __restrict__ cert) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    double s = 0, eb = 0, et = 0;
+    for (int j = lane; j < dim; j += 32) {
+        const float v = x[r * dim + j];
+        double t, e;
+        s += (double)v * v;
+        va::cert_elem(v, 1.0, VA_CERT_BF16, t, e);
+        eb += e * e;
+        va::cert_elem(v, 1.0, VA_CERT_TF32, t, e);
+        et += e * e;
+    }
+    s = warp_sum_d(s);
+    eb = warp_sum_d(eb);
+    et = warp_sum_d(et);
+    if (lane == 0) {
+        atomicMax(cert, __float_as_uint(__double2float_ru(sqrt(s))));
+        atomicMax(cert + 1 + VA_CERT_BF16, __float_as_uint(__double2float_ru(sqrt(eb) * (1.0 + 1e-12))));
+        atomicMax(cert + 1 + VA_CERT_TF32, __float_as_uint(__double2float_ru(sqrt(et) * (1.0 + 1e-12))));
+    }
+}
+
+template <class T>
+__global__ void k_gather_rows_t(const T* __restrict__ src, int width, const uint32_t* __restrict__ rows, int64_t n,
+                                T* __restrict__ dst) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * width; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / width;
+        dst[i] = src[(int64_t)rows[r] * width + (i - r * width)];
+    }
+}
+
+__global__ void k_scatter_rows(const float* __restrict__ v, const uint32_t* __restrict__ ids,
+                               const uint32_t* __restrict__ rows, int64_t n, int k, float* __restrict__ out_v,
+                               uint32_t* __restrict__ out_i) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * k; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / k;
+        const int64_t o = (int64_t)rows[r] * k + (i - r * k);
+        out_v[o] = v[i];
+        out_i[o] = ids[i];
+    }
+}
+
 // Probe-rank bucket of pair i: its rank (the rank-th nearest centroid), ranks >= nb - 1 together.
 __device__ __forceinline__ int rank_bucket(int64_t i, int nprobe, int nb) { return min((int)(i % nprobe), nb - 1); }
 
@@ -264,7 +313,12 @@ __global__ void k_probe_scatter(const uint32_t* __restrict__ probes, int64_t m, 
 
 // One block per query: the `pool` best approximate keys among its nprobe lists of kp candidates
 // (positions in list order), their exact squared L2 (fp64 of the fp32 rows), the k best by
-// (distance, original id), sorted.
+// (distance, original id), sorted. Certificate (the flat search's, va_search.cu certify): every
+// row of the probed lists outside the pool has an approximate key >= T, the pool's largest
+// (a (query, probe) list drops only keys at or above its last, and the per-query bound never cuts
+// into the pool), and |key - (|x|^2 - 2 q.x)| <= eps for every row; when the k-th exact key plus
+// eps stays below T the k best of the probed lists are exact. Otherwise the query is appended to
+// fail_list (no output) and rescanned exactly.
 constexpr int MR_THREADS = 256;
 __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __restrict__ q, int dim,
                                                                  const int64_t* __restrict__ ginv, int nprobe,
@@ -272,11 +326,17 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
                                                                  const uint32_t* __restrict__ pi, int kp, int pool,
                                                                  int k, const float* __restrict__ rows,
                                                                  const uint32_t* __restrict__ ids,
-                                                                 float* __restrict__ out_v,
-                                                                 uint32_t* __restrict__ out_i) {
+                                                                 const uint32_t* __restrict__ cert, int cert_kind,
+                                                                 int dpad, float* __restrict__ out_v,
+                                                                 uint32_t* __restrict__ out_i,
+                                                                 uint32_t* __restrict__ fail_list,
+                                                                 uint32_t* __restrict__ fail_cnt) {
     __shared__ uint64_t s_sel[128];
     __shared__ uint64_t s_ex[128];
     __shared__ va::SelectShared sh;
+    __shared__ unsigned long long s_t;
+    __shared__ double s_qn2, s_an, s_ae;
+    __shared__ int s_ok;
     const int64_t qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     auto get = [&](int64_t i) -> uint64_t {
@@ -286,8 +346,31 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
         if (id == va::kInvalidId) return ~0ull;
         return va::composite(va::f2key(pk[o]), id);
     };
+    if (threadIdx.x == 0) s_t = 0;
     const int m = va::block_select_radix((int64_t)nprobe * kp, pool, get, s_sel, sh);
     __syncthreads();
+    {
+        unsigned long long t = 0;
+        for (int i = threadIdx.x; i < m; i += blockDim.x) t = s_sel[i] > t ? s_sel[i] : t;
+        if (m < pool) t = ~0ull;
+        atomicMax(&s_t, t);
+    }
+    if (warp == 0 && cert) {
+        double a = 0, e2 = 0;
+        for (int j = lane; j < dim; j += 32) {
+            double t, err;
+            va::cert_elem(q[qi * dim + j], 1.0, cert_kind, t, err);
+            a += t * t;
+            e2 += err * err;
+        }
+        a = warp_sum_d(a);
+        e2 = warp_sum_d(e2);
+        if (lane == 0) {
+            s_qn2 = a;
+            s_an = sqrt(a) * (1.0 + 1e-12);
+            s_ae = sqrt(e2) * (1.0 + 1e-12);
+        }
+    }
     for (int c = warp; c < m; c += MR_THREADS / 32) {
         const uint64_t sc = s_sel[c];
         uint64_t comp = ~0ull;
@@ -306,6 +389,24 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
     const int p2 = va::next_pow2(m > 0 ? m : 1);
     for (int i = m + threadIdx.x; i < p2; i += blockDim.x) s_ex[i] = ~0ull;
     va::block_bitonic_sort(s_ex, p2);
+    if (cert && s_t != ~0ull) {
+        if (threadIdx.x == 0) {
+            const double u24 = 5.9604644775390625e-08, u22 = 2.384185791015625e-07;
+            const double vk = (double)va::key2f((uint32_t)(s_ex[k - 1] >> 32));
+            const double dk = vk * (1.0 + 4.0 * u24) - s_qn2 * (1.0 - 1e-12);
+            const double mb = (double)__uint_as_float(cert[0]), md = (double)__uint_as_float(cert[1 + cert_kind]);
+            const double A = s_an + s_ae, g = (double)dpad * u22;
+            double eps = 2.0 * (A * md + s_ae * mb + g * A * (mb + md)) +
+                         u24 * (2.0 * A * (mb + md) * (1.0 + g) + mb * mb) + 2.0 * u24 * mb * mb;
+            eps = eps * (1.0 + 1e-6) + 1e-30;
+            s_ok = dk + eps < (double)va::key2f((uint32_t)(s_t >> 32)) ? 1 : 0;
+        }
+        __syncthreads();
+        if (!s_ok) {
+            if (threadIdx.x == 0) fail_list[atomicAdd(fail_cnt, 1u)] = (uint32_t)qi;
+            return;
+        }
+    }
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
         const uint64_t c = i < m ? s_ex[i] : ~0ull;
         out_v[qi * k + i] = c == ~0ull ? INFINITY : va::key2f((uint32_t)(c >> 32));
@@ -411,6 +512,15 @@ int prepare_operand(va_context* ctx, va_ivf* ivf) {
     k_row_norms<<<(unsigned)(((n + 512) * 32 + 255) / 256), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, n + 512,
                                                                                   ivf->bias);
     VA_TRY(va_check_launch("k_row_norms"));
+    if (cudaMalloc((void**)&ivf->cert, VA_CERT_WORDS * 4) != cudaSuccess) {
+        cudaGetLastError();
+        return va_set_error(VA_ERR_OOM, "IVF certificate buffer allocation failed");
+    }
+    VA_CUDA_TRY(cudaMemsetAsync(ivf->cert, 0, VA_CERT_WORDS * 4, ctx->stream));
+    if (n) {
+        k_ivf_row_cert<<<(unsigned)((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(ivf->rows, n, ivf->dim, ivf->cert);
+        VA_TRY(va_check_launch("k_ivf_row_cert"));
+    }
     return va_synchronize(ctx);
 }
 
@@ -764,6 +874,7 @@ int va_ivf_destroy(va_ivf* ivf) {
     if (ivf->op) cudaFree(ivf->op);
     if (ivf->op32 && ivf->op32_owned) cudaFree(ivf->op32);
     if (ivf->bias) cudaFree(ivf->bias);
+    if (ivf->cert) cudaFree(ivf->cert);
     if (ivf->scratch) cudaFree(ivf->scratch);
     if (ivf->h_plan) cudaFreeHost(ivf->h_plan);
     delete ivf;
@@ -968,10 +1079,49 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     a.sync_cnt = nullptr;
     a.sync_words = 0;
     a.limit_ms = 2000u;
+    // Fail count and list of the certificate (context aux buffer: the coarse step is done with it).
+    void* aux;
+    VA_TRY(va_aux_buffer(ctx, 256 + round_up(nq * 4, 256), &aux));
+    uint32_t* fail_cnt = (uint32_t*)aux;
+    uint32_t* fail_list = (uint32_t*)((uint8_t*)aux + 256);
+    VA_CUDA_TRY(cudaMemsetAsync(fail_cnt, 0, 4, ctx->stream));
     VA_TRY(va_tc_filter_lists(ctx, a, n_qtiles, 0, n_qtiles, d_tiles, ivf->offsets, gmap, nprobe, kp, true));
-    k_ivf_merge_rerank<<<(unsigned)nq, MR_THREADS, 0, ctx->stream>>>(queries, ivf->dim, ginv, nprobe, pk, pi, kp, pool,
-                                                                    k, ivf->rows, ivf->ids, out_vals, out_ids);
-    return va_check_launch("k_ivf_merge_rerank");
+    k_ivf_merge_rerank<<<(unsigned)nq, MR_THREADS, 0, ctx->stream>>>(
+        queries, ivf->dim, ginv, nprobe, pk, pi, kp, pool, k, ivf->rows, ivf->ids, ivf->cert,
+        elem == 2 ? VA_CERT_BF16 : VA_CERT_TF32, ivf->dpad, out_vals, out_ids, fail_list, fail_cnt);
+    VA_TRY(va_check_launch("k_ivf_merge_rerank"));
+    // Queries the certificate could not prove: an exact fp64 scan of their probed lists.
+    uint32_t nf = 0;
+    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_sync_one(ctx));
+    ctx->stat_uncertified = nf;
+    ctx->stat_exact = nf;
+    if (!nf) return VA_OK;
+    VA_REQUIRE(nf <= 65535, "%u uncertified IVF queries exceed one exact rescan (65535)", nf);
+    const size_t gq = round_up((int64_t)nf * ivf->dim * 4, 256), gp = round_up((int64_t)nf * nprobe * 4, 256),
+                 lb = (size_t)nprobe * nf * k, rb = round_up((int64_t)nf * k * 4, 256);
+    void* ws2;
+    VA_TRY(va_workspace(ctx, gq + gp + lb * 8 + 2 * rb + 256, &ws2));
+    float* fq = (float*)ws2;
+    uint32_t* fp = (uint32_t*)((uint8_t*)ws2 + gq);
+    float* cv = (float*)((uint8_t*)fp + gp);
+    uint32_t* ci = (uint32_t*)(cv + lb);
+    float* fv = (float*)(ci + lb);
+    uint32_t* fi = (uint32_t*)((uint8_t*)fv + rb);
+    k_gather_rows_t<float><<<grid_for((int64_t)nf * ivf->dim), 256, 0, ctx->stream>>>(queries, ivf->dim, fail_list,
+                                                                                      nf, fq);
+    k_gather_rows_t<uint32_t><<<grid_for((int64_t)nf * nprobe), 256, 0, ctx->stream>>>(probes, nprobe, fail_list, nf,
+                                                                                       fp);
+    VA_TRY(va_check_launch("k_gather_rows_t"));
+    const size_t smem = (size_t)ivf->dim * 4;
+    if (smem > 48 * 1024)
+        VA_CUDA_TRY(cudaFuncSetAttribute(k_ivf_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_ivf_scan<<<dim3((unsigned)nprobe, nf), LS_THREADS, smem, ctx->stream>>>(fq, nf, ivf->dim, fp, nprobe, ivf->rows,
+                                                                              ivf->ids, ivf->offsets, k, cv, ci);
+    VA_TRY(va_check_launch("k_ivf_scan"));
+    VA_TRY(va_merge_lists_internal(ctx, cv, ci, nprobe, (int64_t)nf * k, k, nf, k, VA_SELECT_MIN, fv, fi));
+    k_scatter_rows<<<grid_for((int64_t)nf * k), 256, 0, ctx->stream>>>(fv, fi, fail_list, nf, k, out_vals, out_ids);
+    return va_check_launch("k_scatter_rows");
 }
 
 int va_ivf_search_host(va_context* ctx, const va_ivf* ivf, const float* queries_host, int64_t nq, int k, int nprobe,

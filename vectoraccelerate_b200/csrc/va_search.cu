@@ -685,7 +685,16 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     va_log_info("va_knn_search: %lld queries, pool %d: %u not certified by the first pass", (long long)nq, pool, n1);
     if (!n1) return VA_OK;
     VA_TRY(gather_queries(ctx, queries, db->dim, list1, n1, gq1));
-    const int pool2 = wider_pool(pool);
+    // Few failures: the next list size. More than a quarter of the batch: neighbourhoods denser
+    // than the pool can separate at this precision (clustered data), so a much wider pool (at least
+    // 4x and 512), which later searches of this metric then start with.
+    const bool dense = (int64_t)n1 * 4 > nq;
+    int pool2 = wider_pool(pool);
+    if (dense && pool < VA_MAX_SELECT_K) {
+        pool2 = std::min(std::max(4 * pool, 512), VA_MAX_SELECT_K);
+        if (nq >= 64) db->pool_hint[metric] = std::max(db->pool_hint[metric], (pool2 + k - 1) / k);
+    }
+    va_log_info("va_knn_search: second pass over %u queries with a pool of %d", n1, pool2);
     if (pool2) {
         VA_TRY(tc_pass(ctx, db, gq1, n1, k, metric, elem, pool2, gv1, gi1, list2, cnt + 32, false));
         uint32_t n2 = 0;
@@ -896,6 +905,9 @@ int va_knn_search_local(va_context* ctx, const va_database* cdb, const float* qu
         ctx->stat_exact = nq;
         VA_TRY(search_exact(ctx, db, queries, nq, k, metric, out_vals, out_ids));
     } else {
+        // A pool this database learned it needs for this metric (dense neighbourhoods).
+        if (db->pool_hint[metric] > 0)
+            pool = std::max(pool, (int)std::min<int64_t>((int64_t)db->pool_hint[metric] * k, VA_MAX_SELECT_K));
         const int elem = prec == VA_PREC_TF32 ? 4 : 2;
         VA_TRY(search_tc(ctx, db, queries, nq, k, metric, elem, pool, out_vals, out_ids));
     }

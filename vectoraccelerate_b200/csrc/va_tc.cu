@@ -15,8 +15,9 @@
 //                 exact integer distance for int8 / bit codes) with the biases broadcast by
 //                 shuffles, and keeps a sorted list of each query's KP best (key, id) in shared
 //                 memory. A warp-uniform test per 64-column chunk skips the lists; otherwise the
-//                 candidates are inserted one at a time by the whole warp (few candidates) or by
-//                 every lane into its own row at once (many)
+//                 candidates are inserted one at a time by the whole warp (few candidates) or,
+//                 when the chunk has many, every lane sorts its own row's candidates and merges
+//                 them into its list from the back (all lanes at once)
 //
 // Every (query tile, row split) item starts its lists empty, so without help each item would
 // re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share a bound per
@@ -222,12 +223,12 @@ __device__ __forceinline__ void tmem_wait64(uint32_t (&r)[64]) {
 // ids li[r*KP + j], j < KP, sorted by (key, id). The 32 lanes of a warp update one row's list
 // together: lane l holds entries l, l + 32, ... (E = KP / 32 per lane).
 //
-// Row stride of the candidate lists in shared memory: KP + 1 for KP <= 64, so that both one row
-// read by the whole warp (warp-cooperative insertion) and 32 rows read one entry each (per-lane
-// insertion) touch 32 different banks; 128-entry lists keep stride KP (no per-lane mode), their
-// shared memory being needed for pipeline stages.
+// Row stride of the candidate lists in shared memory: KP + 1, so that both one row read by the
+// whole warp (warp-cooperative insertion) and 32 rows read one entry each (per-lane merge) touch
+// 32 different banks. (128-entry lists with stride 129 still leave room for the stages the
+// kernels had with stride 128: 2 single-CTA stages, 3 pair stages.)
 template <int KP>
-constexpr int list_stride() { return KP <= 64 ? KP + 1 : KP; }
+constexpr int list_stride() { return KP + 1; }
 
 // Insert (key, id) into row r's list (warp-uniform arguments) and return the new KP-th key.
 // The position is the number of entries <= key (candidates arrive in increasing id order, so an
@@ -274,22 +275,51 @@ __device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r
     return __shfl_sync(0xFFFFFFFFu, last, 31);
 }
 
-// Insert (key, id) into this lane's own row list (key below the row's KP-th key): entries
-// greater than key move up one slot from the end (the KP-th drops out), an equal key goes after
-// the entries already there. Returns the new KP-th key.
+// Merge this lane's candidates of one chunk into its own row's list, keeping the KP best by (key,
+// id). The candidates are the chunk columns order[0..c) (keys kk[col], ids id0 + col), sorted by
+// (key, id). The c largest of the union are dropped from the back first, then the survivors are
+// written backward from the list's end, so only the entries above the smallest surviving
+// candidate move: O(c + moved entries) per chunk instead of one shift per candidate. Returns the
+// new KP-th key.
 template <int KP>
-__device__ __forceinline__ float lane_list_insert(float* lk, uint32_t* li, int r, float key, uint32_t id) {
+__device__ __forceinline__ float lane_list_merge(float* lk, uint32_t* li, int r, const float* kk,
+                                                 const uint8_t* order, int c, uint32_t id0) {
     float* k = lk + r * list_stride<KP>();
     uint32_t* d = li + r * list_stride<KP>();
-    int p = KP - 1;
-    for (; p > 0; --p) {
-        const float prev = k[p - 1];
-        if (!(prev > key)) break;
-        k[p] = prev;
-        d[p] = d[p - 1];
+    int ii = KP - 1, jj = c - 1;
+    float lk_i = k[ii];
+    uint32_t ld_i = d[ii];
+    float ck = kk[order[jj]];
+    uint32_t cd = id0 + order[jj];
+    for (int drop = c; drop > 0; --drop) {
+        // drop the larger of the list's and the candidates' largest remaining entry
+        if (jj >= 0 && !(ii >= 0 && (lk_i > ck || (lk_i == ck && ld_i > cd)))) {
+            if (--jj >= 0) {
+                ck = kk[order[jj]];
+                cd = id0 + order[jj];
+            }
+        } else if (--ii >= 0) {
+            lk_i = k[ii];
+            ld_i = d[ii];
+        }
     }
-    k[p] = key;
-    d[p] = id;
+    for (int w = ii + jj + 1; jj >= 0; --w) {
+        if (ii >= 0 && (lk_i > ck || (lk_i == ck && ld_i > cd))) {
+            k[w] = lk_i;
+            d[w] = ld_i;
+            if (--ii >= 0) {
+                lk_i = k[ii];
+                ld_i = d[ii];
+            }
+        } else {
+            k[w] = ck;
+            d[w] = cd;
+            if (--jj >= 0) {
+                ck = kk[order[jj]];
+                cd = id0 + order[jj];
+            }
+        }
+    }
     return k[KP - 1];
 }
 
@@ -333,22 +363,29 @@ __device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bi
 #pragma unroll
         for (int i = 0; i < 64; ++i) kk[i] = __uint_as_float(r[i]);
     }
-    if constexpr (list_stride<KP>() != KP) {
-        // Many candidates in the chunk (a cold list, or a dense pool): each lane inserts its own
-        // candidates into its own row in column order, all lanes at once.
+    {
+        // Many candidates in the chunk (a cold list, or a dense pool): each lane sorts its own
+        // passing candidates (insertion sort by key; equal keys keep column order, i.e. id order)
+        // and merges them into its own row, all lanes at once.
         const unsigned total = __reduce_add_sync(0xFFFFFFFFu, (unsigned)__popcll(pass));
         if (total >= 8u) {
-            while (__any_sync(0xFFFFFFFFu, pass != 0)) {
-                if (pass) {
-                    const int i = __ffsll((long long)pass) - 1;
-                    pass &= pass - 1;
-                    const float key = kk[i];
-                    if (key < thr && id0 + (uint32_t)i < n_rows) {
-                        thr_own = lane_list_insert<KP>(lk, li, row0 + lane, key, id0 + (uint32_t)i);
-                        thr = fminf(thr_own, thr_g);
-                    }
-                }
+            uint8_t order[64];
+            int c = 0;
+            while (pass) {
+                const int i = __ffsll((long long)pass) - 1;
+                pass &= pass - 1;
+                const float key = kk[i];
+                if (!(key < thr && id0 + (uint32_t)i < n_rows)) continue;
+                int q = c;
+                for (; q > 0 && kk[order[q - 1]] > key; --q) order[q] = order[q - 1];
+                order[q] = (uint8_t)i;
+                ++c;
             }
+            if (c) {
+                thr_own = lane_list_merge<KP>(lk, li, row0 + lane, kk, order, c, id0);
+                thr = fminf(thr_own, thr_g);
+            }
+            __syncwarp();
             return;
         }
     }
@@ -1201,7 +1238,7 @@ int launch_filter(va_context* ctx, const TcFilterArgs& a, int stages, size_t sme
 }
 
 size_t smem_bytes(int kp, int stages, bool pair) {
-    const int stride = kp <= 64 ? kp + 1 : kp;  // list_stride<KP>()
+    const int stride = kp + 1;  // list_stride<KP>()
     return 1024 + (size_t)stages * (pair ? PSTAGE_BYTES : STAGE_BYTES) + (size_t)stride * BM * 8 +
            (2 * stages + 5) * 8 + 16;
 }
