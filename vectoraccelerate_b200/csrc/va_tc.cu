@@ -15,9 +15,8 @@
 //                 exact integer distance for int8 / bit codes) with the biases broadcast by
 //                 shuffles, and keeps a sorted list of each query's KP best (key, id) in shared
 //                 memory. A warp-uniform test per 64-column chunk skips the lists; otherwise the
-//                 candidates are inserted one at a time by the whole warp (few candidates) or,
-//                 when the chunk has many, every lane sorts its own row's candidates and merges
-//                 them into its list from the back (all lanes at once)
+//                 candidates are inserted one at a time by the whole warp (few candidates) or by
+//                 every lane into its own row at once (many; lists of every size)
 //
 // Every (query tile, row split) item starts its lists empty, so without help each item would
 // re-insert its first KP candidates and ~KP*ln(rows/KP) more. Items therefore share a bound per
@@ -224,7 +223,7 @@ __device__ __forceinline__ void tmem_wait64(uint32_t (&r)[64]) {
 // together: lane l holds entries l, l + 32, ... (E = KP / 32 per lane).
 //
 // Row stride of the candidate lists in shared memory: KP + 1, so that both one row read by the
-// whole warp (warp-cooperative insertion) and 32 rows read one entry each (per-lane merge) touch
+// whole warp (warp-cooperative insertion) and 32 rows read one entry each (per-lane insertion) touch
 // 32 different banks. (128-entry lists with stride 129 still leave room for the stages the
 // kernels had with stride 128: 2 single-CTA stages, 3 pair stages.)
 template <int KP>
@@ -275,51 +274,22 @@ __device__ __forceinline__ float warp_list_insert(float* lk, uint32_t* li, int r
     return __shfl_sync(0xFFFFFFFFu, last, 31);
 }
 
-// Merge this lane's candidates of one chunk into its own row's list, keeping the KP best by (key,
-// id). The candidates are the chunk columns order[0..c) (keys kk[col], ids id0 + col), sorted by
-// (key, id). The c largest of the union are dropped from the back first, then the survivors are
-// written backward from the list's end, so only the entries above the smallest surviving
-// candidate move: O(c + moved entries) per chunk instead of one shift per candidate. Returns the
-// new KP-th key.
+// Insert (key, id) into this lane's own row list (key below the row's KP-th key): entries
+// greater than key move up one slot from the end (the KP-th drops out), an equal key goes after
+// the entries already there. Returns the new KP-th key.
 template <int KP>
-__device__ __forceinline__ float lane_list_merge(float* lk, uint32_t* li, int r, const float* kk,
-                                                 const uint8_t* order, int c, uint32_t id0) {
+__device__ __forceinline__ float lane_list_insert(float* lk, uint32_t* li, int r, float key, uint32_t id) {
     float* k = lk + r * list_stride<KP>();
     uint32_t* d = li + r * list_stride<KP>();
-    int ii = KP - 1, jj = c - 1;
-    float lk_i = k[ii];
-    uint32_t ld_i = d[ii];
-    float ck = kk[order[jj]];
-    uint32_t cd = id0 + order[jj];
-    for (int drop = c; drop > 0; --drop) {
-        // drop the larger of the list's and the candidates' largest remaining entry
-        if (jj >= 0 && !(ii >= 0 && (lk_i > ck || (lk_i == ck && ld_i > cd)))) {
-            if (--jj >= 0) {
-                ck = kk[order[jj]];
-                cd = id0 + order[jj];
-            }
-        } else if (--ii >= 0) {
-            lk_i = k[ii];
-            ld_i = d[ii];
-        }
+    int p = KP - 1;
+    for (; p > 0; --p) {
+        const float prev = k[p - 1];
+        if (!(prev > key)) break;
+        k[p] = prev;
+        d[p] = d[p - 1];
     }
-    for (int w = ii + jj + 1; jj >= 0; --w) {
-        if (ii >= 0 && (lk_i > ck || (lk_i == ck && ld_i > cd))) {
-            k[w] = lk_i;
-            d[w] = ld_i;
-            if (--ii >= 0) {
-                lk_i = k[ii];
-                ld_i = d[ii];
-            }
-        } else {
-            k[w] = ck;
-            d[w] = cd;
-            if (--jj >= 0) {
-                ck = kk[order[jj]];
-                cd = id0 + order[jj];
-            }
-        }
-    }
+    k[p] = key;
+    d[p] = id;
     return k[KP - 1];
 }
 
@@ -364,28 +334,21 @@ __device__ __forceinline__ void filter_chunk(uint32_t (&r)[64], const float (&bi
         for (int i = 0; i < 64; ++i) kk[i] = __uint_as_float(r[i]);
     }
     {
-        // Many candidates in the chunk (a cold list, or a dense pool): each lane sorts its own
-        // passing candidates (insertion sort by key; equal keys keep column order, i.e. id order)
-        // and merges them into its own row, all lanes at once.
+        // Many candidates in the chunk (a cold list, or a dense pool): each lane inserts its own
+        // candidates into its own row in column order, all lanes at once.
         const unsigned total = __reduce_add_sync(0xFFFFFFFFu, (unsigned)__popcll(pass));
         if (total >= 8u) {
-            uint8_t order[64];
-            int c = 0;
-            while (pass) {
-                const int i = __ffsll((long long)pass) - 1;
-                pass &= pass - 1;
-                const float key = kk[i];
-                if (!(key < thr && id0 + (uint32_t)i < n_rows)) continue;
-                int q = c;
-                for (; q > 0 && kk[order[q - 1]] > key; --q) order[q] = order[q - 1];
-                order[q] = (uint8_t)i;
-                ++c;
+            while (__any_sync(0xFFFFFFFFu, pass != 0)) {
+                if (pass) {
+                    const int i = __ffsll((long long)pass) - 1;
+                    pass &= pass - 1;
+                    const float key = kk[i];
+                    if (key < thr && id0 + (uint32_t)i < n_rows) {
+                        thr_own = lane_list_insert<KP>(lk, li, row0 + lane, key, id0 + (uint32_t)i);
+                        thr = fminf(thr_own, thr_g);
+                    }
+                }
             }
-            if (c) {
-                thr_own = lane_list_merge<KP>(lk, li, row0 + lane, kk, order, c, id0);
-                thr = fminf(thr_own, thr_g);
-            }
-            __syncwarp();
             return;
         }
     }
