@@ -55,6 +55,12 @@ def parse_args():
     p.add_argument("--nq", type=int, default=10_000)
     p.add_argument("--k", type=int, default=10)
     p.add_argument("--precision", choices=["bf16", "tf32", "fp32"], default="bf16")
+    p.add_argument("--filter-precision", choices=["auto", "bf16", "tf32"], default="auto",
+                   help="float configurations other than the headline: the filter precision (auto = the "
+                        "library's PREC_AUTO choice)")
+    p.add_argument("--pool-factor", type=int, default=None,
+                   help="float configurations other than the headline: candidate pool = factor x k "
+                        "(default: the configuration's own rerank factor)")
     p.add_argument("--rerank", type=int, default=0, help="headline: candidate-pool factor (0 = automatic)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the oracle parity check of sampled queries")
@@ -723,12 +729,14 @@ def run_config(a):
     hv = torch.empty((nq, k), dtype=torch.float32).pin_memory()
     hi = torch.empty((nq, k), dtype=torch.int32).pin_memory()
     metric = {"COSINE": va.METRIC_COSINE, "IP": va.METRIC_IP}.get(c.get("metric"), va.METRIC_L2SQ)
+    cprec = {"auto": va.PREC_AUTO, "bf16": va.PREC_BF16, "tf32": va.PREC_TF32}[a.filter_precision]
+    crerank = c.get("rerank", 0) if a.pool_factor is None else a.pool_factor
     final = [lv, li]
 
     # One step = one library call over the whole database (sharded over the ranks for N > 1).
     def search(qptr, ov, oi):
         if kind == "float":
-            _ffi.call("va_knn_search", ctx.handle, db.handle, qptr, nq, k, metric, va.PREC_AUTO, c["rerank"], ov, oi)
+            _ffi.call("va_knn_search", ctx.handle, db.handle, qptr, nq, k, metric, cprec, crerank, ov, oi)
         elif kind == "int8":
             _ffi.call("va_int8_knn_search", ctx.handle, db.handle, qptr, nq, k, c["candidates"], ov, oi)
         else:
@@ -835,7 +843,8 @@ def run_config(a):
             ops = 2.0 * nq * n_local * dim
             if kind == "float":
                 peak, lab, unit = bf16, f"{peak_src} bf16 sustained", "TFLOP/s"
-                prec_used = auto_precision(k, c["rerank"], c["rows"] == "f32")
+                prec_used = (auto_precision(k, crerank, c["rows"] == "f32") if a.filter_precision == "auto"
+                             else a.filter_precision)
                 if prec_used == "tf32":
                     peak, lab = bf16 / 2.0, f"{peak_src} bf16 sustained / 2 for tf32"
             else:

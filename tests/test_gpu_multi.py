@@ -135,13 +135,17 @@ def _run_ranks(mode, world=2):
     for p in procs:
         p.start()
     res = {}
-    for _ in range(world):
-        r, what, secs = out.get(timeout=180)
-        res[r] = (what, secs)
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
+    try:
+        for _ in range(world):
+            r, what, secs = out.get(timeout=180)
+            res[r] = (what, secs)
+    finally:
+        # a rank that never reports must not keep the test process (and its exit) waiting
+        for p in procs:
+            p.join(timeout=60 if len(res) == world else 1)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
     return res
 
 

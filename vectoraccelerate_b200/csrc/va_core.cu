@@ -216,6 +216,33 @@ int va_sync_one(va_context* ctx) {
     return VA_OK;
 }
 
+bool va_host_pinned(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+int va_copy_to_device(va_context* ctx, void* dst_dev, const void* src_host, size_t bytes) {
+    if (!va_host_pinned(src_host)) VA_TRY(va_synchronize(ctx));
+    VA_CUDA_TRY(cudaMemcpyAsync(dst_dev, src_host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return VA_OK;
+}
+
+int va_copy_to_host(va_context* ctx, void* dst_host, const void* src_dev, size_t bytes) {
+    if (!va_host_pinned(dst_host)) VA_TRY(va_synchronize(ctx));
+    VA_CUDA_TRY(cudaMemcpyAsync(dst_host, src_dev, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    return VA_OK;
+}
+
+int va_read_u32(va_context* ctx, const uint32_t* src_dev, uint32_t* out) {
+    VA_TRY(va_sync_one(ctx));
+    VA_CUDA_TRY(cudaMemcpyAsync(out, src_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return va_sync_one(ctx);
+}
+
 extern "C" {
 
 int va_last_gpu_time_ms(va_context* ctx, float* ms) {
@@ -299,7 +326,7 @@ int va_buffer_free(va_context* ctx, void* dptr) {
     VA_REQUIRE(ctx, "ctx must not be NULL");
     if (!dptr) return VA_OK;
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
-    VA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    VA_TRY(va_synchronize(ctx));  // bounded: the stream's work may still use the buffer
     VA_CUDA_TRY(cudaFree(dptr));
     return VA_OK;
 }
@@ -328,16 +355,14 @@ int va_buffer_upload(va_context* ctx, void* dst, const void* src, size_t bytes) 
     VA_REQUIRE(ctx && dst && src, "ctx, dst and src must not be NULL");
     if (!bytes) return VA_OK;
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
-    VA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
-    return VA_OK;
+    return va_copy_to_device(ctx, dst, src, bytes);
 }
 
 int va_buffer_download(va_context* ctx, void* dst, const void* src, size_t bytes) {
     VA_REQUIRE(ctx && dst && src, "ctx, dst and src must not be NULL");
     if (!bytes) return VA_OK;
     VA_CUDA_TRY(cudaSetDevice(ctx->device));
-    VA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
-    return VA_OK;
+    return va_copy_to_host(ctx, dst, src, bytes);
 }
 
 int va_buffer_copy(va_context* ctx, void* dst, const void* src, size_t bytes) {

@@ -467,15 +467,23 @@ void va_group_destroy(va_context* ctx) {
     ctx->group = nullptr;  // members are plain contexts from here on
     const NcclApi* api = nullptr;
     if (nccl(&api) == VA_OK && !g->aborted) {
-        for (int m = 0; m < g->nlocal; ++m) {
-            if (!g->comms[m]) continue;
-            cudaSetDevice(g->members[m]->device);
-            cudaStreamSynchronize(g->members[m]->stream);
-            api->CommFinalize(g->comms[m]);
+        // Bounded wait for the members' streams: a collective still waiting for a peer that has
+        // gone is aborted rather than finalized (finalizing would wait for it).
+        bool idle = true;
+        for (int m = 0; m < g->nlocal; ++m)
+            if (va_sync_one(g->members[m]) != VA_OK) idle = false;
+        if (!idle) {
+            abort_group(g);
+        } else {
+            for (int m = 0; m < g->nlocal; ++m) {
+                if (!g->comms[m]) continue;
+                cudaSetDevice(g->members[m]->device);
+                api->CommFinalize(g->comms[m]);
+            }
+            if (wait_comms(g, "ncclCommFinalize") == VA_OK)
+                for (int m = 0; m < g->nlocal; ++m)
+                    if (g->comms[m]) api->CommDestroy(g->comms[m]);
         }
-        if (wait_comms(g, "ncclCommFinalize") == VA_OK)
-            for (int m = 0; m < g->nlocal; ++m)
-                if (g->comms[m]) api->CommDestroy(g->comms[m]);
     }
     for (int m = 1; m < g->nlocal; ++m) va_context_destroy(g->members[m]);
     delete g;
@@ -693,9 +701,11 @@ int va_db_create_int8_sharded(va_context* ctx, const float* rows, int on_device,
     float* mm[kMaxLocal] = {};
     int s = VA_OK;
     auto cleanup = [&] {
+        // bounded: an exchange still waiting for a peer that has gone is aborted before the frees
+        for (int m = 0; m < g->nlocal; ++m)
+            if (!g->aborted && va_sync_one(g->members[m]) != VA_OK) abort_group(g);
         for (int m = 0; m < g->nlocal; ++m) {
             cudaSetDevice(g->members[m]->device);
-            cudaStreamSynchronize(g->members[m]->stream);
             if (stage[m]) cudaFree(stage[m]);
             if (mm[m]) cudaFree(mm[m]);
         }

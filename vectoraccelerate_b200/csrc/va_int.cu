@@ -403,8 +403,7 @@ int run_int_filter(va_context* ctx, const va_database* db, const TcPlan& plan, c
 int int8_fallback(va_context* ctx, va_database* db, const float* queries, int k, int pool, const uint32_t* fail_list,
                   const uint32_t* fail_cnt, float* gq, float* gv, uint32_t* gi, float* out_vals, uint32_t* out_ids) {
     uint32_t nf = 0;
-    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_TRY(va_sync_one(ctx));
+    VA_TRY(va_read_u32(ctx, fail_cnt, &nf));
     if (!nf) return VA_OK;
     const int dim = db->dim, cpad = db->cpad;
     const int64_t n = db->n;

@@ -92,6 +92,18 @@ int va_sync_one(va_context* ctx);
 int va_group_synchronize(va_context* ctx);
 void va_group_destroy(va_context* ctx);
 
+// Host <-> device copies of the host-buffer entry points. With page-locked host memory
+// (cudaHostAlloc / cudaHostRegister, e.g. torch's pin_memory) the copy is queued asynchronously.
+// A copy from or to pageable memory blocks the calling thread until the stream reaches it, so it
+// is issued only after a bounded wait for the stream (va_synchronize): work held up on the stream
+// (a collective whose peer has gone) then ends the call with VA_ERR_TIMEOUT or VA_ERR_NCCL
+// instead of blocking it for good. A pageable download has landed when the call returns.
+bool va_host_pinned(const void* p);
+int va_copy_to_device(va_context* ctx, void* dst_dev, const void* src_host, size_t bytes);
+int va_copy_to_host(va_context* ctx, void* dst_host, const void* src_dev, size_t bytes);
+// A 32-bit count written by device work on this context's stream (bounded wait, then the copy).
+int va_read_u32(va_context* ctx, const uint32_t* src_dev, uint32_t* out);
+
 // Device staging buffer of at least `bytes` for host-buffer calls.
 int va_io_buffer(va_context* ctx, size_t bytes, void** out);
 // Auxiliary device scratch of at least `bytes` (stream-ordered reuse across calls).

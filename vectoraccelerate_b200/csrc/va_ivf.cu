@@ -1092,8 +1092,7 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_TRY(va_check_launch("k_ivf_merge_rerank"));
     // Queries the certificate could not prove: an exact fp64 scan of their probed lists.
     uint32_t nf = 0;
-    VA_CUDA_TRY(cudaMemcpyAsync(&nf, fail_cnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_TRY(va_sync_one(ctx));
+    VA_TRY(va_read_u32(ctx, fail_cnt, &nf));
     ctx->stat_uncertified = nf;
     ctx->stat_exact = nf;
     if (!nf) return VA_OK;
@@ -1135,10 +1134,10 @@ int va_ivf_search_host(va_context* ctx, const va_ivf* ivf, const float* queries_
     float* dq = (float*)io;
     float* dv = (float*)((uint8_t*)io + round_up((int64_t)qb, 256));
     uint32_t* di = (uint32_t*)((uint8_t*)dv + round_up((int64_t)rb, 256));
-    VA_CUDA_TRY(cudaMemcpyAsync(dq, queries_host, qb, cudaMemcpyHostToDevice, ctx->stream));
+    VA_TRY(va_copy_to_device(ctx, dq, queries_host, qb));
     VA_TRY(va_ivf_search(ctx, ivf, dq, nq, k, nprobe, dv, di));
-    VA_CUDA_TRY(cudaMemcpyAsync(out_vals_host, dv, rb, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_CUDA_TRY(cudaMemcpyAsync(out_ids_host, di, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_copy_to_host(ctx, out_vals_host, dv, rb));
+    VA_TRY(va_copy_to_host(ctx, out_ids_host, di, rb));
     return va_synchronize(ctx);
 }
 

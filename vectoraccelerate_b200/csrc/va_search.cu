@@ -521,8 +521,7 @@ int scatter_results(va_context* ctx, const float* v, const uint32_t* ids, const 
 
 // Count written by a merge (the call waits for the stream: the next passes depend on it).
 int read_count(va_context* ctx, const uint32_t* dcnt, uint32_t* n) {
-    VA_CUDA_TRY(cudaMemcpyAsync(n, dcnt, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    return va_sync_one(ctx);
+    return va_read_u32(ctx, dcnt, n);
 }
 
 // Exact route: the reference's chunked two-pass strategy (executeChunkedTwoPass,
@@ -939,10 +938,10 @@ int va_knn_search_host(va_context* ctx, const va_database* db, const float* quer
     float* dq = (float*)io;
     float* dv = (float*)((uint8_t*)io + round_up((int64_t)qb, 256));
     uint32_t* di = (uint32_t*)((uint8_t*)dv + round_up((int64_t)rb, 256));
-    VA_CUDA_TRY(cudaMemcpyAsync(dq, queries_host, qb, cudaMemcpyHostToDevice, ctx->stream));
+    VA_TRY(va_copy_to_device(ctx, dq, queries_host, qb));
     VA_TRY(va_knn_search(ctx, db, dq, nq, k, metric, precision, rerank, dv, di));
-    VA_CUDA_TRY(cudaMemcpyAsync(out_vals_host, dv, rb, cudaMemcpyDeviceToHost, ctx->stream));
-    VA_CUDA_TRY(cudaMemcpyAsync(out_ids_host, di, rb, cudaMemcpyDeviceToHost, ctx->stream));
+    VA_TRY(va_copy_to_host(ctx, out_vals_host, dv, rb));
+    VA_TRY(va_copy_to_host(ctx, out_ids_host, di, rb));
     VA_TRY(va_synchronize(ctx));
     cudaEventElapsedTime(&ctx->last_ms, ctx->ev_start, ctx->ev_stop);
     return VA_OK;
