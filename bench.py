@@ -932,6 +932,7 @@ def run_ivf(a):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1) / a.steps
+    unc, exa = ctx.last_search_stats()
     t0 = time.perf_counter()
     for _ in range(a.steps):
         _ffi.call("va_ivf_search_host", ctx.handle, h.value, hq.data_ptr(), nq, k, nprobe, hv.data_ptr(),
@@ -963,6 +964,9 @@ def run_ivf(a):
                    "l2_policy": "rows (512 MB) larger than L2, no flush"},
         "e2e": {"value": nq / (e2e_ms * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
                 "d2h_bytes_per_step": nq * k * 8},
+        "exactness": {"uncertified": int(unc), "exact_rescan": int(exa),
+                      "note": "per step: queries whose list-scan pool the certificate could not prove exact "
+                              "(they take the exact fp64 rescan of their probed lists)"},
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

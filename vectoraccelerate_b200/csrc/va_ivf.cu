@@ -330,7 +330,8 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
                                                                  int dpad, float* __restrict__ out_v,
                                                                  uint32_t* __restrict__ out_i,
                                                                  uint32_t* __restrict__ fail_list,
-                                                                 uint32_t* __restrict__ fail_cnt) {
+                                                                 uint32_t* __restrict__ fail_cnt,
+                                                                 const uint32_t* __restrict__ gthr) {
     __shared__ uint64_t s_sel[128];
     __shared__ uint64_t s_ex[128];
     __shared__ va::SelectShared sh;
@@ -371,25 +372,29 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
             s_ae = sqrt(e2) * (1.0 + 1e-12);
         }
     }
-    for (int c = warp; c < m; c += MR_THREADS / 32) {
-        const uint64_t sc = s_sel[c];
-        uint64_t comp = ~0ull;
-        if (sc != ~0ull) {
-            const uint32_t pos = (uint32_t)sc;
-            double acc = 0;
-            for (int j = lane; j < dim; j += 32) {
-                const double t = (double)q[qi * dim + j] - (double)rows[(int64_t)pos * dim + j];
-                acc += t * t;
-            }
-            acc = warp_sum_d(acc);
-            comp = va::composite(va::f2key((float)acc), ids[pos]);
+    // Exact key of one candidate (list position in the low word; warp-collective).
+    auto exact = [&](uint64_t sc) -> uint64_t {
+        if (sc == ~0ull) return ~0ull;
+        const uint32_t pos = (uint32_t)sc;
+        double acc = 0;
+        for (int j = lane; j < dim; j += 32) {
+            const double t = (double)q[qi * dim + j] - (double)rows[(int64_t)pos * dim + j];
+            acc += t * t;
         }
+        acc = warp_sum_d(acc);
+        return va::composite(va::f2key((float)acc), ids[pos]);
+    };
+    for (int c = warp; c < m; c += MR_THREADS / 32) {
+        const uint64_t comp = exact(s_sel[c]);
         if (lane == 0) s_ex[c] = comp;
     }
     const int p2 = va::next_pow2(m > 0 ? m : 1);
     for (int i = m + threadIdx.x; i < p2; i += blockDim.x) s_ex[i] = ~0ull;
     va::block_bitonic_sort(s_ex, p2);
     if (cert && s_t != ~0ull) {
+        __shared__ double s_u;
+        __shared__ unsigned s_lmin;
+        __shared__ int s_next;
         if (threadIdx.x == 0) {
             const double u24 = 5.9604644775390625e-08, u22 = 2.384185791015625e-07;
             const double vk = (double)va::key2f((uint32_t)(s_ex[k - 1] >> 32));
@@ -399,9 +404,58 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
             double eps = 2.0 * (A * md + s_ae * mb + g * A * (mb + md)) +
                          u24 * (2.0 * A * (mb + md) * (1.0 + g) + mb * mb) + 2.0 * u24 * mb * mb;
             eps = eps * (1.0 + 1e-6) + 1e-30;
-            s_ok = dk + eps < (double)va::key2f((uint32_t)(s_t >> 32)) ? 1 : 0;
+            s_u = dk + eps;
+            s_ok = s_u < (double)va::key2f((uint32_t)(s_t >> 32)) ? 1 : 0;
+            s_lmin = 0xFFFFFFFFu;
+            s_next = 0;
         }
         __syncthreads();
+        if (!s_ok) {
+            // Extension (as the flat merge's): every row outside the probed lists' entries was
+            // dropped against the query's bound or a full list's last key, so its key is at least
+            // B = min(next float above the bound, the last key of every full list). If U = D_k
+            // (rounded up) + eps < B, the entries with a key <= U hold every row that can reach
+            // the top k: rerank the ones above the pool too and take the exact top k.
+            for (int sp = threadIdx.x; sp < nprobe; sp += blockDim.x) {
+                const int64_t o = ginv[qi * nprobe + sp] * kp + kp - 1;
+                if (pi[o] != va::kInvalidId) atomicMin(&s_lmin, va::f2key(pk[o]));
+            }
+            __syncthreads();
+            float B = s_lmin == 0xFFFFFFFFu ? INFINITY : va::key2f(s_lmin);
+            const uint32_t bnd = gthr ? gthr[qi] : 0xFFFFFFFFu;
+            if (bnd != 0xFFFFFFFFu) B = fminf(B, nextafterf(va::key2f(bnd), INFINITY));
+            const double U = s_u;
+            if (U < (double)B) {
+                __syncthreads();  // s_sel (the pool) is read no more: it takes the extension
+                for (int64_t i = threadIdx.x; i < (int64_t)nprobe * kp; i += blockDim.x) {
+                    const uint64_t c = get(i);
+                    if (c != ~0ull && c > s_t && (double)va::key2f((uint32_t)(c >> 32)) <= U) {
+                        const int slot = atomicAdd(&s_next, 1);
+                        if (slot < 128) s_sel[slot] = c;
+                    }
+                }
+                __syncthreads();
+                const int m2 = s_next;
+                if (m2 <= 128) {
+                    for (int c = warp; c < 128; c += MR_THREADS / 32) {
+                        const uint64_t comp = exact(c < m2 ? s_sel[c] : ~0ull);
+                        if (lane == 0) s_sel[c] = comp;
+                    }
+                    va::block_bitonic_sort(s_sel, 128);
+                    __syncthreads();
+                    if (threadIdx.x == 0) {
+                        // the k smallest of the two sorted lists (s_ex: p2 entries, s_sel: 128)
+                        int a = 0, b = 0;
+                        uint64_t outk[128];
+                        for (int i = 0; i < k; ++i)
+                            outk[i] = (b >= 128 || (a < p2 && s_ex[a] < s_sel[b])) ? s_ex[a++] : s_sel[b++];
+                        for (int i = 0; i < k; ++i) s_ex[i] = outk[i];
+                        s_ok = 1;
+                    }
+                    __syncthreads();
+                }
+            }
+        }
         if (!s_ok) {
             if (threadIdx.x == 0) fail_list[atomicAdd(fail_cnt, 1u)] = (uint32_t)qi;
             return;
@@ -1088,7 +1142,7 @@ int va_ivf_search(va_context* ctx, const va_ivf* civf, const float* queries, int
     VA_TRY(va_tc_filter_lists(ctx, a, n_qtiles, 0, n_qtiles, d_tiles, ivf->offsets, gmap, nprobe, kp, true));
     k_ivf_merge_rerank<<<(unsigned)nq, MR_THREADS, 0, ctx->stream>>>(
         queries, ivf->dim, ginv, nprobe, pk, pi, kp, pool, k, ivf->rows, ivf->ids, ivf->cert,
-        elem == 2 ? VA_CERT_BF16 : VA_CERT_TF32, ivf->dpad, out_vals, out_ids, fail_list, fail_cnt);
+        elem == 2 ? VA_CERT_BF16 : VA_CERT_TF32, ivf->dpad, out_vals, out_ids, fail_list, fail_cnt, gthr);
     VA_TRY(va_check_launch("k_ivf_merge_rerank"));
     // Queries the certificate could not prove: an exact fp64 scan of their probed lists.
     uint32_t nf = 0;

@@ -156,8 +156,8 @@ struct CertArgs {
 // and the shared bound never cuts into the pool), hence D(y) >= T - eps. If the k-th exact key
 // D_k (from the fp64 rerank, rounded up) satisfies D_k + eps < T, no dropped row can reach the
 // top k: the result is the exact top k. Otherwise the query goes to the fail list.
-__device__ __forceinline__ bool certify(const CertArgs& ca, int metric, float vk, double qn2, double a_norm,
-                                        double a_err, float T) {
+__device__ __forceinline__ double cert_bound(const CertArgs& ca, int metric, float vk, double qn2, double a_norm,
+                                            double a_err) {
     const double u24 = 5.9604644775390625e-08, u22 = 2.384185791015625e-07;
     double dk;  // upper bound of the k-th exact key
     if (metric == VA_METRIC_L2SQ)
@@ -177,7 +177,7 @@ __device__ __forceinline__ bool certify(const CertArgs& ca, int metric, float vk
     else
         eps += u24 * A * (mb + md) * (1.0 + g);
     eps = eps * (1.0 + 1e-6) + 1e-30;
-    return dk + eps < (double)T;
+    return dk + eps;
 }
 
 __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
@@ -297,13 +297,10 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
     }
     __syncthreads();
     const int mode = metric == VA_METRIC_IP ? 1 : 0;
-    for (int c = warp; c < kp2; c += nwarps) {
-        uint64_t comp = c < m ? sel[c] : ~0ull;
-        uint32_t id = (uint32_t)comp;
-        if (comp == ~0ull || id == va::kInvalidId) {
-            if (lane == 0) ex[c] = ~0ull;
-            continue;
-        }
+    // Exact key of one candidate (warp-collective; every lane returns it).
+    auto exact = [&](uint64_t comp) -> uint64_t {
+        const uint32_t id = (uint32_t)comp;
+        if (comp == ~0ull || id == va::kInvalidId) return ~0ull;
         const int64_t base = (int64_t)id * dim;
         double s = 0, xx = 0;
         if ((dim & 127) == 0) {
@@ -346,28 +343,79 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         }
         if (metric == VA_METRIC_COSINE) xx = warp_sum_d(xx);
         s = warp_sum_d(s);
-        if (lane == 0) {
-            float v;
-            if (metric == VA_METRIC_L2SQ || metric == VA_METRIC_IP) {
-                v = (float)s;
-            } else {
-                double den = s_qn * sqrt(xx);
-                double sim = den > 0 ? s / den : 0.0;
-                sim = fmin(1.0, fmax(-1.0, sim));
-                v = (float)(1.0 - sim);
-            }
-            ex[c] = va::composite(va::mode_key(v, mode), id);
+        float v;
+        if (metric == VA_METRIC_L2SQ || metric == VA_METRIC_IP) {
+            v = (float)s;
+        } else {
+            double den = s_qn * sqrt(xx);
+            double sim = den > 0 ? s / den : 0.0;
+            sim = fmin(1.0, fmax(-1.0, sim));
+            v = (float)(1.0 - sim);
         }
+        return va::composite(va::mode_key(v, mode), id);
+    };
+    for (int c = warp; c < kp2; c += nwarps) {
+        const uint64_t r = exact(c < m ? sel[c] : ~0ull);
+        if (lane == 0) ex[c] = r;
     }
     va::block_bitonic_sort(ex, kp2);
     if (ca.on && T != ~0ull) {
         // The pool holds at least pool_n >= k valid candidates here, so ex[k - 1] is the k-th.
-        __shared__ int s_ok;
+        __shared__ int s_ok, s_next;
+        __shared__ double s_u;
+        __shared__ unsigned s_lmin;
         if (threadIdx.x == 0) {
             const float vk = va::mode_val((uint32_t)(ex[k - 1] >> 32), mode);
-            s_ok = certify(ca, metric, vk, s_qn2, s_an, s_ae, va::key2f((uint32_t)(T >> 32))) ? 1 : 0;
+            s_u = cert_bound(ca, metric, vk, s_qn2, s_an, s_ae);
+            s_ok = s_u < (double)va::key2f((uint32_t)(T >> 32)) ? 1 : 0;
+            s_lmin = 0xFFFFFFFFu;
+            s_next = 0;
         }
         __syncthreads();
+        if (!s_ok && n_pool <= MR_POOL) {
+            // Extension. U = D_k (rounded up) + eps bounds the key of every row that can reach the
+            // top k. Every row outside the collected candidates has a key of at least
+            // B = min(next float above the shared bound, the last key of every full list): the
+            // filter dropped it against the bound or a full list's threshold, or it sits in a list
+            // above the bound. If U < B, the candidates with a key <= U (the pool plus the few
+            // collected ones between T and U) contain every row with a key <= U, so their exact
+            // top k is the exact answer: a row left out has D >= K - eps > U - eps = D_k, which is
+            // >= the k-th exact distance of the larger set. No second filter pass is needed.
+            for (int sp = threadIdx.x; sp < splits; sp += blockDim.x) {
+                const int64_t off = ((int64_t)sp * nq_pad + qi) * kp + kp - 1;
+                if (part_ids[off] != va::kInvalidId) atomicMin(&s_lmin, va::f2key(part_keys[off]));
+            }
+            __syncthreads();
+            float B = s_lmin == 0xFFFFFFFFu ? INFINITY : va::key2f(s_lmin);
+            if (bound != 0xFFFFFFFFu) B = fminf(B, nextafterf(va::key2f(bound), INFINITY));
+            const double U = s_u;
+            if (U < (double)B) {
+                // the collected candidates above the pool with a key <= U, into sel (kp2 slots)
+                for (int i = threadIdx.x; i < n_pool; i += blockDim.x)
+                    if (pool[i] > T && (double)va::key2f((uint32_t)(pool[i] >> 32)) <= U) {
+                        const int slot = atomicAdd(&s_next, 1);
+                        if (slot < kp2) sel[slot] = pool[i];
+                    }
+                __syncthreads();
+                const int m2 = s_next;
+                if (m2 <= kp2) {
+                    for (int c = warp; c < kp2; c += nwarps) {
+                        const uint64_t r = exact(c < m2 ? sel[c] : ~0ull);
+                        if (lane == 0) sel[c] = r;
+                    }
+                    va::block_bitonic_sort(sel, kp2);
+                    __syncthreads();
+                    if (threadIdx.x == 0) {
+                        // the k smallest of the two sorted lists, into pool (no longer needed)
+                        int a = 0, b = 0;
+                        for (int i = 0; i < k; ++i) pool[i] = (b >= kp2 || (a < kp2 && ex[a] < sel[b])) ? ex[a++] : sel[b++];
+                        for (int i = 0; i < k; ++i) ex[i] = pool[i];
+                        s_ok = 1;
+                    }
+                    __syncthreads();
+                }
+            }
+        }
         if (!s_ok) {
             if (threadIdx.x == 0) fail_list[atomicAdd(fail_cnt, 1u)] = (uint32_t)qi;
             return;
