@@ -5,7 +5,10 @@ exactly and certifies per query that no row outside the pool can enter the top k
 bound of the keys' rounding error against the gap between the k-th exact distance and the pool's
 last key). Runs of near-duplicate rows closer together than that bound defeat the certificate on
 purpose: those queries must take the second tensor-core pass (wider pool) or the exact route, and
-the results must still equal the oracle's (CPUTopK.swift:62-79: exact sum((q - x)^2) order)."""
+the results must still equal the oracle's (CPUTopK.swift:62-79: exact sum((q - x)^2) order).
+When more than 1/32 of a batch fails, the second pass widens the pool to at least 512 and the
+database keeps it (dense neighbourhoods); the tests of the narrow fallbacks use batches where the
+few failing queries stay under that share."""
 
 import numpy as np
 import pytest
@@ -15,12 +18,12 @@ from test_gpu_parity import _check
 pytestmark = pytest.mark.gpu
 
 
-def _near_duplicate_db(n, d, dup, seed, spread=1e-3, normalize=False):
-    """n random rows plus, for each of the first 4 queries, `dup` rows within `spread` of one point
-    near that query (the query's top k lie inside the run)."""
+def _near_duplicate_db(n, d, dup, seed, spread=1e-3, normalize=False, nq=64):
+    """n random rows plus, for each of the first 4 of `nq` queries, `dup` rows within `spread` of
+    one point near that query (the query's top k lie inside the run)."""
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((n, d)).astype(np.float32)
-    q = rng.standard_normal((64, d)).astype(np.float32)
+    q = rng.standard_normal((nq, d)).astype(np.float32)
     runs = []
     for i in range(4):
         p = q[i] + 0.5 * rng.standard_normal(d).astype(np.float32)
@@ -45,8 +48,9 @@ def _search(ctx, x, q, k, metric=0, precision=0, rerank=0, dtype=0):
 @pytest.mark.parametrize("metric", [0, 1, 2])
 @pytest.mark.parametrize("precision", [2, 3])
 def test_runs_beyond_every_pool_take_the_exact_route(ctx, oracle, metric, precision):
-    # 300 near-duplicates: neither the first pool (32) nor the second (64) separates them.
-    x, q = _near_duplicate_db(20_000, 128, 300, seed=11 + metric, normalize=metric == 1)
+    # 300 near-duplicates: neither the first pool (32) nor the second (64) separates them. Four
+    # failing queries of 200 (under 1/32 of the batch) keep the second pass at the next list size.
+    x, q = _near_duplicate_db(20_000, 128, 300, seed=11 + metric, normalize=metric == 1, nq=200)
     vals, ids, (unc, exact) = _search(ctx, x, q, 10, metric=metric, precision=precision)
     assert unc >= 4 and exact >= 4, (unc, exact)
     _check(oracle, q, x, 10, metric, vals, ids)
@@ -54,7 +58,7 @@ def test_runs_beyond_every_pool_take_the_exact_route(ctx, oracle, metric, precis
 
 def test_runs_inside_the_second_pool_are_certified_there(ctx, oracle):
     # 50 near-duplicates: the first pool (32) cannot separate them, the second (64) holds them all.
-    x, q = _near_duplicate_db(20_000, 128, 50, seed=5)
+    x, q = _near_duplicate_db(20_000, 128, 50, seed=5, nq=200)
     vals, ids, (unc, exact) = _search(ctx, x, q, 10, precision=3)
     assert unc >= 4 and exact == 0, (unc, exact)
     _check(oracle, q, x, 10, 0, vals, ids)
@@ -62,7 +66,7 @@ def test_runs_inside_the_second_pool_are_certified_there(ctx, oracle):
 
 def test_bf16_rows_exact_route(ctx, oracle):
     # bf16 rows: the exact route reads the bf16 rows widened exactly
-    x, q = _near_duplicate_db(10_000, 128, 300, seed=3, normalize=True)
+    x, q = _near_duplicate_db(10_000, 128, 300, seed=3, normalize=True, nq=200)
     xb = oracle.f32_to_bf16(x)
     vals, ids, (unc, exact) = _search(ctx, xb, q, 10, metric=2, precision=3, dtype=1)
     assert exact >= 4

@@ -132,6 +132,7 @@ __global__ void k_operand(const void* src, int dtype, int64_t n_valid, int64_t n
 // original rows, emit the top k sorted by (distance, id).
 constexpr int MR_THREADS = 256;
 constexpr int MR_POOL = 1024;  // candidates kept in shared memory after the bound test
+constexpr int MR_VEC = 6;      // 16-byte row loads in flight per lane in the exact rerank
 
 // Exactness certificate of one reduced-precision pass (see k_merge_rerank).
 struct CertArgs {
@@ -180,7 +181,7 @@ __device__ __forceinline__ double cert_bound(const CertArgs& ca, int metric, flo
     return dk + eps;
 }
 
-__global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __restrict__ part_keys,
+__global__ void __launch_bounds__(MR_THREADS, 3) k_merge_rerank(const float* __restrict__ part_keys,
                                                            const uint32_t* __restrict__ part_ids, int splits,
                                                            int64_t nq_pad, int kp, int pool_n,
                                                            const float* __restrict__ queries,
@@ -304,28 +305,40 @@ __global__ void __launch_bounds__(MR_THREADS) k_merge_rerank(const float* __rest
         const int64_t base = (int64_t)id * dim;
         double s = 0, xx = 0;
         if ((dim & 127) == 0) {
-            // 16-byte (fp32) or 8-byte (bf16) loads of four consecutive elements per lane: the
-            // row's loads are independent and in flight together.
-#pragma unroll 4
-            for (int j0 = lane * 4; j0 < dim; j0 += 128) {
-                const float4 qv = *(const float4*)(sq + j0);
-                float4 xv;
-                if (dtype == VA_DTYPE_BF16) {
-                    const uint2 u = __ldg((const uint2*)((const uint16_t*)rows + base + j0));
-                    xv = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-                } else {
-                    xv = __ldg((const float4*)((const float*)rows + base + j0));
-                }
-                const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            // 16-byte (fp32) or 8-byte (bf16) loads of four consecutive elements per lane, issued
+            // in batches of MR_VEC per lane before any of them is used: a row of up to
+            // 128 * MR_VEC dimensions is one memory round trip (the gathered rows are
+            // latency-bound, not bandwidth-bound).
+            for (int j00 = 0; j00 < dim; j00 += 128 * MR_VEC) {
+                float4 xv[MR_VEC];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    if (metric == VA_METRIC_L2SQ) {
-                        const double t = (double)qa[e] - (double)xa[e];
-                        s += t * t;
-                    } else {
-                        s += (double)qa[e] * (double)xa[e];
-                        xx += (double)xa[e] * (double)xa[e];
+                for (int v = 0; v < MR_VEC; ++v) {
+                    const int j0 = j00 + 128 * v + lane * 4;
+                    if (j0 < dim) {
+                        if (dtype == VA_DTYPE_BF16) {
+                            const uint2 u = __ldg((const uint2*)((const uint16_t*)rows + base + j0));
+                            xv[v] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                                __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+                        } else {
+                            xv[v] = __ldg((const float4*)((const float*)rows + base + j0));
+                        }
+                    }
+                }
+#pragma unroll
+                for (int v = 0; v < MR_VEC; ++v) {
+                    const int j0 = j00 + 128 * v + lane * 4;
+                    if (j0 >= dim) break;
+                    const float4 qv = *(const float4*)(sq + j0);
+                    const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, xa[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (metric == VA_METRIC_L2SQ) {
+                            const double t = (double)qa[e] - (double)xa[e];
+                            s += t * t;
+                        } else {
+                            s += (double)qa[e] * (double)xa[e];
+                            xx += (double)xa[e] * (double)xa[e];
+                        }
                     }
                 }
             }
@@ -732,10 +745,13 @@ int search_tc(va_context* ctx, va_database* db, const float* queries, int64_t nq
     va_log_info("va_knn_search: %lld queries, pool %d: %u not certified by the first pass", (long long)nq, pool, n1);
     if (!n1) return VA_OK;
     VA_TRY(gather_queries(ctx, queries, db->dim, list1, n1, gq1));
-    // Few failures: the next list size. More than a quarter of the batch: neighbourhoods denser
-    // than the pool can separate at this precision (clustered data), so a much wider pool (at least
-    // 4x and 512), which later searches of this metric then start with.
-    const bool dense = (int64_t)n1 * 4 > nq;
+    // Few failures: the next list size. More than 1/32 of the batch: neighbourhoods denser than
+    // the pool can separate at this precision (clustered data), so a much wider pool (at least 4x
+    // and 512), which later searches of this metric then start with. (The second pass runs whole
+    // query tiles over the whole database, so it costs about the failing fraction of the first;
+    // a wider first pool costs a few percent of the filter: C3 with 20% failing spent 83 ms per
+    // batch in second passes against 9 ms for the wider pool.)
+    const bool dense = (int64_t)n1 * 32 > nq;
     int pool2 = wider_pool(pool);
     if (dense && pool < VA_MAX_SELECT_K) {
         pool2 = std::min(std::max(4 * pool, 512), VA_MAX_SELECT_K);
