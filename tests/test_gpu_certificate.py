@@ -113,3 +113,24 @@ def test_dense_neighbourhoods_widen_the_pool_and_are_remembered(ctx, oracle):
         _check(oracle, q, x, 10, 0, vals, ids)
     finally:
         db.close()
+
+
+@pytest.mark.parametrize("metric", [0, 2])
+def test_merge_extension_certifies_without_a_second_pass(ctx, oracle, metric):
+    # 40 near-duplicates per run (more than the pool of 32, closer together than the key error)
+    # spread over the row splits: the pool test fails for those queries, but every split's list
+    # ends far above them, so the merge reranks the whole run and certifies in the first pass.
+    import vectoraccelerate_b200 as va
+    rng = np.random.default_rng(41 + metric)
+    q = rng.standard_normal((200, 128)).astype(np.float32)
+    runs = [q[i] + 0.5 * rng.standard_normal(128).astype(np.float32) for i in range(4)]
+    x = np.concatenate([rng.standard_normal((30_000, 128)).astype(np.float32)] +
+                       [p[None, :] + 1e-3 * rng.standard_normal((40, 128)).astype(np.float32) for p in runs])
+    x = np.ascontiguousarray(x[rng.permutation(len(x))])
+    db = va.Database(ctx, x)
+    try:
+        vals, ids = va.knn_search_host(ctx, db, q, 10, metric, va.PREC_BF16)
+        assert ctx.last_search_stats() == (0, 0)
+        _check(oracle, q, x, 10, metric, vals, ids)
+    finally:
+        db.close()
