@@ -471,6 +471,7 @@ __global__ void __launch_bounds__(MR_THREADS) k_ivf_merge_rerank(const float* __
 // ---------------------------------------------------------------------------------- list scan
 constexpr int LS_THREADS = 256;
 constexpr int LS_BUF = 1024;
+constexpr int LS_ROWS = 4;  // rows per warp and pass of the exact list scan
 
 // One block per (probe, query): exact squared L2 of the query to every row of its probe-th list
 // (a warp per row, fp64 accumulation), the k best (distance, id) composites kept through a
@@ -515,26 +516,60 @@ __global__ void __launch_bounds__(LS_THREADS) k_ivf_scan(const float* __restrict
         }
         __syncthreads();
     };
-    for (int64_t base = r0; base < r1; base += nwarps) {
-        const int64_t r = base + warp;
-        if (r < r1) {
-            double s = 0;
-            for (int j = lane; j < dim; j += 32) {
-                const double t = (double)s_q[j] - (double)rows[r * dim + j];
-                s += t * t;
+    // Each warp takes LS_ROWS rows per pass (rows base + warp + nwarps * u) and issues all of
+    // their loads before using any: the scan is latency-bound on the row reads.
+    const bool vec = (dim & 3) == 0;  // 16-byte loads: rows and the query start on 16 bytes
+    for (int64_t base = r0; base < r1; base += (int64_t)nwarps * LS_ROWS) {
+        double acc[LS_ROWS];
+#pragma unroll
+        for (int u = 0; u < LS_ROWS; ++u) acc[u] = 0;
+        if (vec) {
+            for (int j0 = lane * 4; j0 < dim; j0 += 128) {
+                float4 xv[LS_ROWS];
+#pragma unroll
+                for (int u = 0; u < LS_ROWS; ++u) {
+                    const int64_t r = base + warp + (int64_t)nwarps * u;
+                    xv[u] = r < r1 ? __ldg((const float4*)(rows + r * dim + j0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                const float4 qv = *(const float4*)(s_q + j0);
+#pragma unroll
+                for (int u = 0; u < LS_ROWS; ++u) {
+                    const double t0 = (double)qv.x - (double)xv[u].x, t1 = (double)qv.y - (double)xv[u].y;
+                    const double t2 = (double)qv.z - (double)xv[u].z, t3 = (double)qv.w - (double)xv[u].w;
+                    acc[u] += t0 * t0 + t1 * t1 + t2 * t2 + t3 * t3;
+                }
             }
-            s = warp_sum_d(s);
-            if (lane == 0) {
-                const uint64_t comp = va::composite(va::f2key((float)s), ids[r]);
-                if (comp < s_thr) {
-                    const int slot = atomicAdd(&s_cnt, 1);
-                    if (slot < LS_BUF) s_buf[slot] = comp;
+        } else {
+#pragma unroll
+            for (int u = 0; u < LS_ROWS; ++u) {
+                const int64_t r = base + warp + (int64_t)nwarps * u;
+                double a = 0;
+                if (r < r1)
+                    for (int j = lane; j < dim; j += 32) {
+                        const double t = (double)s_q[j] - (double)rows[r * dim + j];
+                        a += t * t;
+                    }
+                acc[u] = a;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < LS_ROWS; ++u) acc[u] = warp_sum_d(acc[u]);
+        if (lane == 0) {
+#pragma unroll
+            for (int u = 0; u < LS_ROWS; ++u) {
+                const int64_t r = base + warp + (int64_t)nwarps * u;
+                if (r < r1) {
+                    const uint64_t comp = va::composite(va::f2key((float)acc[u]), ids[r]);
+                    if (comp < s_thr) {
+                        const int slot = atomicAdd(&s_cnt, 1);
+                        if (slot < LS_BUF) s_buf[slot] = comp;
+                    }
                 }
             }
         }
         __syncthreads();
         // Every thread reads the count before any warp of the next pass over rows adds to it.
-        const bool full = s_cnt > LS_BUF - nwarps;
+        const bool full = s_cnt > LS_BUF - nwarps * LS_ROWS;
         __syncthreads();
         if (full) compact();
     }
