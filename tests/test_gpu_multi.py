@@ -102,6 +102,19 @@ def _rank_worker(rank, world, nid, mode, out):
         x = rng.standard_normal((50_001, 64)).astype(np.float32)
         q = rng.standard_normal((100, 64)).astype(np.float32)
         r0, cnt = ctx.shard_range(len(x))
+        if mode == "int8":
+            # each rank's rows on its own device; the library all-reduces the coding range
+            import torch
+            rows = torch.from_numpy(x[r0:r0 + cnt]).to(f"cuda:{rank}")
+            db = va.ShardedDatabase(ctx, device_ptr=rows.data_ptr(), n=len(x), dim=64, kind="int8")
+            dq = ctx.get_buffer_for(q)
+            ov = ctx.get_buffer(100 * 10 * 4, np.float32, (100, 10))
+            oi = ctx.get_buffer(100 * 10 * 4, np.uint32, (100, 10))
+            va._ffi.call("va_int8_knn_search", ctx.handle, db.handle, dq.ptr, 100, 10, 100, ov.ptr, oi.ptr)
+            out.put((rank, (ov.download(), oi.download()), 0.0))
+            db.close()
+            ctx.close()
+            return
         db = va.ShardedDatabase(ctx, x[r0:r0 + cnt], n=len(x), dim=64)
         vals, ids = va.knn_search_host(ctx, db, q, 10)
         if mode == "leaves" and rank == 1:
@@ -158,6 +171,23 @@ def test_rank_contexts_match_the_oracle(oracle):
     for r in (0, 1):
         vals, ids = res[r][0]
         _check(oracle, q, x, 10, 0, vals, ids)
+
+
+@needs2
+def test_rank_contexts_int8_match_the_oracle(oracle):
+    # int8 database sharded over rank contexts from device rows: both range reductions in one
+    # NCCL group (a non-blocking communicator takes one call at a time)
+    res = _run_ranks("int8")
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((50_001, 64)).astype(np.float32)
+    q = rng.standard_normal((100, 64)).astype(np.float32)
+    mins, scales = oracle.sq_perdim_params(x)
+    qc, xc = oracle.sq_perdim_quantize(q, mins, scales), oracle.sq_perdim_quantize(x, mins, scales)
+    tids, tvals, _, _ = oracle.int8_knn(qc, q, xc, x, 100, 10)
+    for r in (0, 1):
+        vals, ids = res[r][0]
+        np.testing.assert_array_equal(ids, tids)
+        np.testing.assert_allclose(vals, tvals, rtol=1e-6)
 
 
 @needs2

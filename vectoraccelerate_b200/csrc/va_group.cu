@@ -740,19 +740,16 @@ int va_db_create_int8_sharded(va_context* ctx, const float* rows, int on_device,
         s = va_sq_perdim_minmax(c, dev, cnt, dim, mm[m], mm[m] + dim);
     }
     if (s == VA_OK && g->nranks > 1) {
-        if (g->nlocal > 1) s = group_start(api);
+        // Both reductions in one group, also with one local member: a non-blocking communicator
+        // takes no second call while the first is still being enqueued.
+        s = group_start(api);
         for (int m = 0; m < g->nlocal && s == VA_OK; ++m) {
             cudaSetDevice(g->members[m]->device);
-            ncclResult_t r1 = api->AllReduce(mm[m], mm[m], (size_t)dim, ncclFloat32, ncclMin, g->comms[m],
-                                             g->members[m]->stream);
-            ncclResult_t r2 = api->AllReduce(mm[m] + dim, mm[m] + dim, (size_t)dim, ncclFloat32, ncclMax, g->comms[m],
-                                             g->members[m]->stream);
-            if (g->nlocal == 1) {
-                s = check_nccl(g, r1, "ncclAllReduce(min)");
-                if (s == VA_OK) s = check_nccl(g, r2, "ncclAllReduce(max)");
-            }
+            api->AllReduce(mm[m], mm[m], (size_t)dim, ncclFloat32, ncclMin, g->comms[m], g->members[m]->stream);
+            api->AllReduce(mm[m] + dim, mm[m] + dim, (size_t)dim, ncclFloat32, ncclMax, g->comms[m],
+                           g->members[m]->stream);
         }
-        if (s == VA_OK && g->nlocal > 1) s = check_nccl(g, api->GroupEnd(), "ncclAllReduce(range)");
+        if (s == VA_OK) s = check_nccl(g, api->GroupEnd(), "ncclAllReduce(range)");
     }
     std::vector<va_database*> sh((size_t)g->nlocal, nullptr);
     for (int m = 0; m < g->nlocal && s == VA_OK; ++m) {
