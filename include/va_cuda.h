@@ -204,8 +204,12 @@ int va_db_compact(va_context* ctx, va_database* db, const uint8_t* keep, int64_t
  * Exactness: the reduced-precision keys only choose a candidate pool, which is reranked exactly;
  * a per-query certificate (a rigorous bound of the keys' rounding error against the gap between
  * the k-th exact distance and the pool's last key) proves that no row outside the pool can enter
- * the top k. Queries that fail it take a second tensor-core pass with a 4x wider pool, and what
- * that cannot certify takes the exact SIMT route, so every result is the exact top k.
+ * the top k; where the pool's last key is too close, the candidates the filter kept beyond the
+ * pool (below the last key of every full list and the shared bound) are reranked too. Queries
+ * that still fail take a second tensor-core pass with a wider pool (the next list size, or at
+ * least 4x and 512 when more than 1/32 of the batch fails; the database then keeps that pool for
+ * the metric), and what that cannot certify takes the exact SIMT route, so every result is the
+ * exact top k.
  * The tensor-core route reads back the count of uncertified queries, so the call waits for the
  * stream once (twice when a second pass runs). A context serves one host thread at a time (its
  * scratch buffers are shared by its calls). */
