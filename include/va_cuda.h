@@ -124,7 +124,9 @@ int va_buffer_alloc(va_context* ctx, size_t bytes, void** dptr);
 int va_buffer_free(va_context* ctx, void* dptr);
 int va_host_alloc(va_context* ctx, size_t bytes, void** hptr); /* pinned host memory */
 int va_host_free(va_context* ctx, void* hptr);
-/* Stream-ordered copies (host<->device or device<->device); asynchronous for pinned memory. */
+/* Stream-ordered copies (host<->device or device<->device); asynchronous for page-locked host
+ * memory. With pageable host memory the call first waits (bounded, as va_synchronize) for the
+ * stream, then copies: it returns when the copy is done, or with VA_ERR_TIMEOUT / VA_ERR_NCCL. */
 int va_buffer_upload(va_context* ctx, void* dst_dev, const void* src_host, size_t bytes);
 int va_buffer_download(va_context* ctx, void* dst_host, const void* src_dev, size_t bytes);
 int va_buffer_copy(va_context* ctx, void* dst_dev, const void* src_dev, size_t bytes);
